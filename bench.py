@@ -1,0 +1,353 @@
+"""Benchmark: fp32-accurate matmul TFLOP/s on B200 (square 8192^3 GEMM).
+
+Workload: C = A @ B, A and B [8192, 8192] fp32 ~ U(-1, 1). The rows of A (and
+so of C) are split across the N ranks (one process per GPU), B is replicated,
+and when N > 1 the C rows are all-gathered over NCCL so every GPU holds C.
+Work is fixed as N grows ("strong" scaling). Default mode 3xTF32
+(fp32-accurate); --mode tf32 times the fast mode.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode 3xtf32|tf32]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference ...   # the reference's CPU matmul, host cores
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SIZE = 8192
+METRIC = "fp32-accurate matmul TFLOP/s & % TF32 roofline at 1/2/4/8 B200 vs host CPU"
+UNIT = "TFLOP/s"
+WORKLOAD = "square fp32 GEMM 8192x8192x8192, rows of A sharded over the GPUs, C rows all-gathered"
+
+# DRAM bytes (read + write) of one launch of the GEMM kernel from the ncu
+# capture summarised in profiles/ (null until that capture exists).
+NCU_TRAFFIC_BYTES_PER_LAUNCH = {"3xtf32": None, "tf32": None}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--mode", choices=["3xtf32", "tf32"], default="3xtf32")
+    p.add_argument("--size", type=int, default=SIZE)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), \
+            float(d["hbm_gbs"]), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ CPU side
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def reference_cpu_sample(n, rows_per_core, cores, seed=4):
+    """Times the reference's own CPU matmul (oracle/_ref, compiled from the
+    reference sources) on `cores` processes, each multiplying its own
+    rows_per_core rows of A by the full B. Falls back to the C restatement
+    (one thread) when the reference build is absent. Returns (tflops, kind,
+    cores_used, seconds, rows)."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_bridge as ob
+    rows = rows_per_core * cores
+    A = ob.seeded_uniform((rows, n), seed)
+    B = ob.seeded_uniform((n, n), seed + 1000)
+    C = np.empty((rows, n), np.float32)
+    if ob.ref_available():
+        lib = ob.ref()
+        t0 = time.perf_counter()
+        rc = lib.ref_matmul_rows_mp(ob._ptr(C), ob._ptr(A), ob._ptr(B), rows, n, n, cores)
+        dt = time.perf_counter() - t0
+        if rc != 0:
+            raise RuntimeError(f"reference row-sliced matmul failed ({rc})")
+        kind, used = "reference", cores
+    else:
+        rows = rows_per_core
+        t0 = time.perf_counter()
+        C = ob.oracle_matmul(A[:rows], B)
+        dt = time.perf_counter() - t0
+        kind, used = "port", 1
+    flops = 2.0 * rows * n * n
+    return flops / dt / 1e12, kind, used, dt, rows
+
+
+def run_reference_arm(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return 0
+    n = args.size
+    cores = cpu_cores()
+    rows_per_core = 8
+    vals = []
+    kind = "reference"
+    used = cores
+    rows = rows_per_core * cores
+    for i in range(args.warmup + args.steps):
+        v, kind, used, dt, rows = reference_cpu_sample(n, rows_per_core, cores, seed=4 + i)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    sample = (f"{rows} rows of A x full B[{n},{n}] per step ({rows_per_core} rows per process, "
+              f"{used} processes), the reference's Functional::matmul CPU loop")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference CPU RNG, U(-1,1))",
+        "config": {"workload": WORKLOAD, "size": n, "mode": "fp32 (reference CPU loop)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ GPU side
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    rank, local_rank, world = env_rank()
+    if world != args.gpus:
+        print(f"--gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+        return 2
+    n = args.size
+    if n % world != 0:
+        print("size must divide evenly over the ranks", file=sys.stderr)
+        return 2
+
+    # CPU baseline first, before any CUDA call in this process.
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cores = cpu_cores()
+        v, kind, used, dt, rows = reference_cpu_sample(n, 8, cores)
+        cpu = {"value": v, "unit": UNIT, "cores": used, "kind": kind,
+               "sample": f"{rows} rows of A x full B[{n},{n}] ({2.0 * rows * n * n / 1e9:.1f} GFLOP) "
+                         f"in {dt:.2f} s over {used} processes"}
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    import macrograd_b200 as mg
+    from macrograd_b200 import _lib, functional as F
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    lib = mg.load()
+    mode = _lib.MG_MODE_TF32X3 if args.mode == "3xtf32" else _lib.MG_MODE_TF32
+    _lib.check(lib.mg_set_mode(mode))
+
+    rows = n // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    A = torch.empty(rows, n, device=dev).uniform_(-1, 1, generator=g)
+    g.manual_seed(4321)
+    B = torch.empty(n, n, device=dev).uniform_(-1, 1, generator=g)
+    C_local = torch.empty(rows, n, device=dev)
+    C_full = torch.empty(n, n, device=dev) if world > 1 else C_local
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        F.matmul(A, B, out=C_local)
+        if world > 1:
+            dist.all_gather_into_tensor(C_full, C_local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, device-timed with events on the launching stream
+    clocks = ClockSampler(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = lib.mg_launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    kern_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+    ev0.record(stream)
+    for i in range(args.steps):
+        kern_ev[i][0].record(stream)
+        F.matmul(A, B, out=C_local)
+        kern_ev[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(C_full, C_local)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    launches = lib.mg_launch_count() - launches0
+    clk = clocks.stop()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in kern_ev)
+
+    t = torch.tensor([elapsed_ms, kern_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, kern_ms = float(t[0]), float(t[1])
+    ms_per_step = elapsed_ms / args.steps
+    flops = 2.0 * n * n * n
+    value = flops / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the public API from pinned host memory
+    e2e = None
+    if not args.no_e2e:
+        A_h = A.cpu().pin_memory()
+        C_h = torch.empty(rows, n, dtype=torch.float32).pin_memory()
+        A_d = torch.empty_like(A)
+
+        def e2e_step():
+            A_d.copy_(A_h, non_blocking=True)
+            F.matmul(A_d, B, out=C_local)
+            if world > 1:
+                dist.all_gather_into_tensor(C_full, C_local)
+            C_h.copy_(C_local, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        te = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e_ms = float(te[0]) / args.steps
+        e2e = {"value": flops / (e_ms * 1e-3) / 1e12, "unit": UNIT,
+               "h2d_bytes_per_step": int(A_h.numel() * 4 * world),
+               "d2h_bytes_per_step": int(C_h.numel() * 4 * world),
+               "ms_per_step": e_ms,
+               "note": "per step: A row shard host->device (pinned), GEMM, all-gather, "
+                       "own C rows device->host; B resident like weights"}
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    bf16, bf16_sus, hbm, src = peaks()
+    tf32_peak = bf16 / 2.0
+    peak = tf32_peak / 3.0 if args.mode == "3xtf32" else tf32_peak
+    per_launch_flops = 2.0 * rows * n * n
+    achieved = per_launch_flops / (kern_ms * 1e-3) / 1e12
+    traffic = NCU_TRAFFIC_BYTES_PER_LAUNCH.get(args.mode)
+    if traffic is not None and world > 1:
+        traffic = traffic / world
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic U(-1,1) (torch generator, seeded), resident in HBM",
+        "config": {"workload": WORKLOAD, "size": n, "rows_per_gpu": rows,
+                   "mode": args.mode, "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "l2": "inputs larger than L2 (2 x 268 MB operands, 268 MB output)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": (f"{src} bf16 dense {bf16:.1f} TFLOP/s / 2 = TF32 {tf32_peak:.1f}"
+                                     + (" / 3 products per fp32-accurate term" if args.mode == "3xtf32" else "")),
+                     "kernel": "mg_gemm_tc_kernel", "kernel_ms": kern_ms},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

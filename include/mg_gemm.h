@@ -1,0 +1,164 @@
+/*
+ * mg_gemm.h -- C ABI of the B200 (sm_100a) GEMM library that replaces the
+ * matmul hot path of Macrograd (MiquelNasarre/macrograd).
+ *
+ * The reference seam is the pair of device entry points
+ *   kernel_ops::matmul       macrograd/include/cuda_backend.h:173
+ *                            (body macrograd/kernels/cuda_backend.cu:3548-3759)
+ *   kernel_ops::matmul_bias  macrograd/include/cuda_backend.h:174
+ *                            (body macrograd/kernels/cuda_backend.cu:3761-4004)
+ * called from Functional::matmul (macrograd/source/tensor_ops.cpp:4596, :4836)
+ * and, through it, from the MatMulOp / MatMulBiasOp backward
+ * (tensor_ops.cpp:4504-4517, :4723-4737). mg_matmul / mg_matmul_bias take the
+ * same arguments (Shape objects flattened to int32 arrays) and keep the same
+ * preconditions; mg_gemm is the general strided form under both.
+ *
+ * Plain C: pointers, sizes and status codes only. No call aborts; every
+ * failure returns an mg_status and mg_last_error() describes it. All work is
+ * enqueued on the caller's stream; no call synchronises the host except
+ * mg_device_status() and the set-up calls.
+ */
+#ifndef MG_GEMM_H
+#define MG_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum mg_status {
+    MG_OK = 0,
+    MG_ERR_INVALID = 1,      /* bad arguments: shapes, ranks, pointers, strides */
+    MG_ERR_UNSUPPORTED = 2,  /* valid request this build cannot run (e.g. no sm_100 device) */
+    MG_ERR_CUDA = 3,         /* a CUDA runtime / driver call failed */
+    MG_ERR_ALLOC = 4,        /* the workspace allocator returned NULL */
+    MG_ERR_TIMEOUT = 5,      /* a kernel wait ran out its time limit (device status) */
+    MG_ERR_NO_KERNEL = 6     /* the library has no kernel image for this device */
+} mg_status;
+
+/* Arithmetic of the tensor-core contraction.
+ *   MG_MODE_TF32X3: fp32-accurate. Each fp32 operand x is split into
+ *     hi = x with its low 13 mantissa bits cleared and lo = x - hi; the
+ *     accumulator receives hi*hi + hi*lo + lo*hi on the TF32 tensor cores.
+ *     The default.
+ *   MG_MODE_TF32: one TF32 product per term (fast mode, ~1e-3 relative).
+ * The reference computes in strict FP32 (CUBLAS_COMPUTE_32F,
+ * cuda_backend.cu:3644); TF32X3 is the mode that matches it within 1e-5. */
+typedef enum mg_mode {
+    MG_MODE_TF32X3 = 0,
+    MG_MODE_TF32 = 1,
+    MG_MODE_DEFAULT = -1     /* use the library mode (mg_set_mode / MG_GEMM_MODE) */
+} mg_mode;
+
+/* Epilogue flags, combined with |. */
+enum {
+    MG_EPI_BIAS = 1,         /* + bias[m*bias_rs + n*bias_cs] (+ per-batch offset) */
+    MG_EPI_CAUSAL = 2,       /* element (m, n) with n > m becomes -inf before softmax */
+    MG_EPI_SOFTMAX = 4       /* row softmax over n (requires N <= 256) */
+};
+
+#define MG_MAX_BATCH_DIMS 6
+
+/* General strided GEMM, in elements:
+ *   C[b][m][n] = alpha * sum_k op(A)[b][m][k] * op(B)[b][k][n]
+ *              (+ bias) (+ beta * C[b][m][n])     then optional row softmax.
+ * op(A) is A stored [M][K] with row stride lda (trans_a = 0) or stored [K][M]
+ * (trans_a = 1); op(B) is B stored [K][N] (trans_b = 0) or [N][K] (trans_b = 1).
+ * The batch index b runs over batch[0..batch_rank) (row-major); an operand's
+ * stride 0 on a dim broadcasts it there. Operands are fp32 device memory. */
+typedef struct mg_gemm_desc {
+    int32_t M, N, K;
+    int32_t trans_a, trans_b;
+    int64_t lda, ldb, ldc;
+    int32_t batch_rank;
+    int32_t batch[MG_MAX_BATCH_DIMS];
+    int64_t a_batch_stride[MG_MAX_BATCH_DIMS];
+    int64_t b_batch_stride[MG_MAX_BATCH_DIMS];
+    int64_t c_batch_stride[MG_MAX_BATCH_DIMS];
+    int64_t bias_batch_stride[MG_MAX_BATCH_DIMS];
+    int64_t bias_rs, bias_cs;  /* bias row / column strides (0 = broadcast) */
+    float alpha;               /* scale on the product (1 for matmul) */
+    float beta;                /* 0: overwrite C; 1: accumulate into C */
+    int32_t epilogue;          /* MG_EPI_* flags */
+    int32_t mode;              /* mg_mode */
+} mg_gemm_desc;
+
+/* Fills a descriptor for a plain row-major C[M][N] = op(A) op(B), batch 1. */
+void mg_gemm_desc_init(mg_gemm_desc* d, int32_t M, int32_t N, int32_t K,
+                       int32_t trans_a, int32_t trans_b);
+
+/* Runs one described GEMM on `stream` (a cudaStream_t; NULL = legacy default). */
+mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* B,
+                  const float* bias, void* stream);
+
+/* Replaces kernel_ops::matmul (cuda_backend.h:173, cuda_backend.cu:3548).
+ * Shapes are the rank-equalised shapes Functional::matmul passes
+ * (tensor_ops.cpp:4547-4579): `rank` >= 2 entries each; A_shape and B_shape
+ * are the STORAGE shapes (before the transpose flags); leading dims are equal
+ * or 1; out_shape = [max(A_i, B_i)..., M, N]. All tensors contiguous fp32.
+ * `out` is overwritten (the reference's out is zero-filled and written with
+ * beta = 0, cuda_backend.cu:3554-3555). */
+mg_status mg_matmul(float* out, const float* A, const float* B,
+                    const int32_t* out_shape, const int32_t* A_shape,
+                    const int32_t* B_shape, int32_t rank, int32_t trans_a,
+                    int32_t trans_b, void* stream);
+
+/* Replaces kernel_ops::matmul_bias (cuda_backend.h:174, cuda_backend.cu:3761).
+ * bias_shape is rank-equalised to `rank`; each dim equals out's or is 1
+ * (tensor_ops.cpp:4807-4818). Any such bias is fused into the epilogue. */
+mg_status mg_matmul_bias(float* out, const float* A, const float* B, const float* bias,
+                         const int32_t* out_shape, const int32_t* A_shape,
+                         const int32_t* B_shape, const int32_t* bias_shape,
+                         int32_t rank, int32_t trans_a, int32_t trans_b, void* stream);
+
+/* Fused attention-score product: out = softmax_rows(alpha * op(A) op(B) (+ bias)
+ * (+ causal mask)), i.e. what the reference's MultiHeadSelfAttention computes
+ * with Functional::matmul(Q / sqrt(d), K, mask, false, true) followed by
+ * Tensor::softmax(-1) (mini_shakespeare/include/transformer.h:233-234,
+ * tensor_ops.cpp:2034-2121). Shapes as mg_matmul_bias; bias may be NULL
+ * (bias_shape ignored then). `causal` applies -inf strictly above the diagonal
+ * (Functional::causal_mask, tensor_ops.cpp:5468-5492). Requires N <= 256. */
+mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const float* bias,
+                            const int32_t* out_shape, const int32_t* A_shape,
+                            const int32_t* B_shape, const int32_t* bias_shape,
+                            int32_t rank, int32_t trans_a, int32_t trans_b,
+                            float alpha, int32_t causal, void* stream);
+
+/* Workspace allocator, stream-ordered like the reference's MemPool
+ * (cuda_backend.h:63-79: cudaMallocAsync / cudaFreeAsync on the library
+ * stream). The library asks for scratch only on paths that need it (operands
+ * whose row stride is not a multiple of 16 bytes are re-laid out there).
+ * Passing NULL functions restores the default (cudaMallocAsync on the call's
+ * stream). The allocator replaces MemPool::allocate/free for the workspace. */
+typedef void* (*mg_alloc_fn)(size_t bytes, void* stream, void* ctx);
+typedef void (*mg_free_fn)(void* ptr, void* stream, void* ctx);
+void mg_set_allocator(mg_alloc_fn alloc_fn, mg_free_fn free_fn, void* ctx);
+
+/* Library default mode (initially from env MG_GEMM_MODE=3xtf32|tf32, else TF32X3). */
+mg_status mg_set_mode(int32_t mode);
+int32_t mg_get_mode(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* mg_last_error(void);
+
+/* Reads (and with reset != 0 clears) the device-side status word of the
+ * current device: MG_OK, or MG_ERR_TIMEOUT when a kernel's bounded wait ran
+ * out (the kernel then skipped its remaining work and exited cleanly).
+ * Synchronises the device. `detail` (may be NULL) receives a code naming the
+ * wait that gave up. */
+mg_status mg_device_status(int32_t* detail, int32_t reset);
+
+/* Number of kernel launches the library has issued in this process
+ * (all devices). For accounting in benchmarks. */
+uint64_t mg_launch_count(void);
+
+/* Library version string. */
+const char* mg_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MG_GEMM_H */

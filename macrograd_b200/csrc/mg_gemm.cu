@@ -1,0 +1,700 @@
+// mg_gemm.cu -- host side and C ABI of the sm_100a GEMM library.
+//
+// Replaces kernel_ops::matmul / kernel_ops::matmul_bias of Macrograd
+// (macrograd/kernels/cuda_backend.cu:3548-4004). Where the reference builds
+// cuBLASLt descriptors, a heuristic cache and per-batch pointer arrays
+// (cuda_backend.cu:3556-3719), this library maps every operand onto a TMA
+// tensor map whose extra dimensions carry the batch (stride-0 dims simply do
+// not appear), and launches one persistent tcgen05 kernel per call.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "mg_gemm.h"
+#include "mg_gemm_kernel.cuh"
+
+namespace {
+
+// ---------------------------------------------------------------- state
+thread_local std::string g_last_error;
+std::atomic<int32_t> g_mode{-2};                 // -2: not read from env yet
+std::atomic<uint64_t> g_launches{0};
+mg_alloc_fn g_alloc = nullptr;
+mg_free_fn g_free = nullptr;
+void* g_alloc_ctx = nullptr;
+std::mutex g_mu;
+
+__device__ int g_device_status[2];
+
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    bool ready = false;
+    int sm_count = 0;
+    int max_smem = 0;
+    size_t attr_smem[3] = {0, 0, 0};   // dynamic smem opted in, per tile width
+    int* status = nullptr;   // device address of g_device_status
+};
+DeviceState g_dev[kMaxDevices];
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+mg_status fail(mg_status s, const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return s;
+}
+
+#define MG_CUDA_TRY(call)                                                                   \
+    do {                                                                                    \
+        cudaError_t e_ = (call);                                                            \
+        if (e_ != cudaSuccess)                                                              \
+            return fail(MG_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));      \
+    } while (0)
+
+int32_t resolve_default_mode()
+{
+    int32_t m = g_mode.load();
+    if (m != -2) return m;
+    int32_t v = MG_MODE_TF32X3;
+    if (const char* e = std::getenv("MG_GEMM_MODE")) {
+        if (!std::strcmp(e, "tf32") || !std::strcmp(e, "TF32") || !std::strcmp(e, "1xtf32")) v = MG_MODE_TF32;
+    }
+    int32_t expect = -2;
+    g_mode.compare_exchange_strong(expect, v);
+    return g_mode.load();
+}
+
+template <int BN>
+constexpr auto kernel_of()
+{
+    return &mg::mg_gemm_tc_kernel<BN>;
+}
+
+int bn_slot(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : 2); }
+
+mg_status device_state(DeviceState** out)
+{
+    int dev = 0;
+    MG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(MG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    DeviceState& d = g_dev[dev];
+    if (!d.ready) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!d.ready) {
+            cudaDeviceProp prop;
+            MG_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
+            if (prop.major != 10)
+                return fail(MG_ERR_UNSUPPORTED,
+                            "device %d is sm_%d%d; this library is built for sm_100a (B200) only",
+                            dev, prop.major, prop.minor);
+            d.sm_count = prop.multiProcessorCount;
+            d.max_smem = (int)prop.sharedMemPerBlockOptin;
+            void* sp = nullptr;
+            MG_CUDA_TRY(cudaGetSymbolAddress(&sp, g_device_status));
+            d.status = static_cast<int*>(sp);
+            if (g_encode == nullptr) {
+                void* fn = nullptr;
+                cudaDriverEntryPointQueryResult q;
+                MG_CUDA_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+                if (q != cudaDriverEntryPointSuccess || fn == nullptr)
+                    return fail(MG_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
+                g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+            }
+            d.ready = true;
+        }
+    }
+    *out = &d;
+    return MG_OK;
+}
+
+// ---------------------------------------------------------------- helpers
+struct Operand {
+    const float* ptr;
+    int64_t rows, cols;       // stored matrix (cols contiguous)
+    int64_t ld;               // elements between stored rows
+    int64_t bs[MG_MAX_BATCH_DIMS];
+};
+
+// Mapping of an operand's batch dims onto at most 3 extra tensor-map dims.
+struct BatchMap {
+    int nmap = 0;
+    int64_t extent[3] = {1, 1, 1};
+    int64_t stride[3] = {0, 0, 0};   // elements
+    int8_t map[MG_MAX_BATCH_DIMS];
+    int32_t mult[MG_MAX_BATCH_DIMS];
+};
+
+// Innermost batch dim first; stride-0 dims are broadcast and get no map dim;
+// a dim whose stride continues the current map dim (stride == map stride *
+// extent so far) merges into it (mixed-radix coordinate).
+bool build_batch_map(int nbd, const int32_t* bsize, const int64_t* bs, BatchMap* bm)
+{
+    for (int d = 0; d < MG_MAX_BATCH_DIMS; ++d) { bm->map[d] = -1; bm->mult[d] = 0; }
+    bm->nmap = 0;
+    for (int d = nbd - 1; d >= 0; --d) {
+        if (bs[d] == 0 || bsize[d] == 1) continue;
+        const int j = bm->nmap - 1;
+        if (j >= 0 && bs[d] == bm->stride[j] * bm->extent[j] &&
+            bm->extent[j] * (int64_t)bsize[d] < (1ll << 31)) {
+            bm->map[d] = (int8_t)j;
+            bm->mult[d] = (int32_t)bm->extent[j];
+            bm->extent[j] *= bsize[d];
+        } else {
+            if (bm->nmap == 3) return false;
+            bm->map[d] = (int8_t)bm->nmap;
+            bm->mult[d] = 1;
+            bm->extent[bm->nmap] = bsize[d];
+            bm->stride[bm->nmap] = bs[d];
+            bm->nmap++;
+        }
+    }
+    return true;
+}
+
+bool tma_compatible(const Operand& x, const BatchMap& bm)
+{
+    if (reinterpret_cast<uintptr_t>(x.ptr) & 15u) return false;
+    if ((x.ld * 4) % 16 != 0) return false;
+    for (int j = 0; j < bm.nmap; ++j)
+        if ((bm.stride[j] * 4) % 16 != 0) return false;
+    if (x.cols >= (1ll << 31) || x.rows >= (1ll << 31)) return false;
+    return true;
+}
+
+mg_status encode_map(CUtensorMap* map, const Operand& x, const BatchMap& bm, int box_rows_is_k,
+                     uint32_t box_outer)
+{
+    // dims: {cols (contiguous), rows, batch map dims...}
+    cuuint64_t dims[5];
+    cuuint64_t strides[4];
+    cuuint32_t box[5];
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    const int rank = 2 + bm.nmap;
+    dims[0] = (cuuint64_t)x.cols;
+    dims[1] = (cuuint64_t)x.rows;
+    strides[0] = (cuuint64_t)(x.ld * 4);
+    for (int j = 0; j < bm.nmap; ++j) {
+        dims[2 + j] = (cuuint64_t)bm.extent[j];
+        strides[1 + j] = (cuuint64_t)(bm.stride[j] * 4);
+        box[2 + j] = 1;
+    }
+    box[0] = 32;
+    box[1] = box_rows_is_k ? 32u : box_outer;
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
+                          const_cast<float*>(x.ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MG_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return MG_OK;
+}
+
+// ---------------------------------------------------------------- aux kernels
+// Copies every distinct batch element of an operand into a dense buffer whose
+// rows are padded to a multiple of 4 floats (16 bytes), so a TMA map can read
+// it. Used only for operands whose own strides break TMA's 16-byte rules
+// (e.g. the vocab-65 logits of the character model: rows of 260 bytes).
+struct PadParams {
+    const float* src;
+    float* dst;
+    int64_t rows, cols, src_ld, dst_ld;
+    int nd;
+    int64_t size[MG_MAX_BATCH_DIMS];
+    int64_t sstride[MG_MAX_BATCH_DIMS];
+};
+
+__global__ void pad_copy_kernel(PadParams p)
+{
+    const int64_t row_global = blockIdx.x;   // over nbatch * rows
+    const int64_t b = row_global / p.rows;
+    const int64_t r = row_global - b * p.rows;
+    int64_t rem = b, soff = 0;
+    for (int d = p.nd - 1; d >= 0; --d) {
+        const int64_t i = rem % p.size[d];
+        rem /= p.size[d];
+        soff += i * p.sstride[d];
+    }
+    const float* s = p.src + soff + r * p.src_ld;
+    float* o = p.dst + row_global * p.dst_ld;
+    for (int64_t c = threadIdx.x; c < p.dst_ld; c += blockDim.x) o[c] = c < p.cols ? s[c] : 0.f;
+}
+
+// K == 0: C = bias (+ beta C), or the softmax of the bias / mask alone.
+struct FillParams {
+    int M, N, nbd;
+    int bsize[MG_MAX_BATCH_DIMS];
+    float* C;
+    int64_t ldc, c_bs[MG_MAX_BATCH_DIMS];
+    const float* bias;
+    int64_t bias_rs, bias_cs, bias_bs[MG_MAX_BATCH_DIMS];
+    float beta;
+    int epi;
+    int64_t rows_total;
+};
+
+__global__ void k0_fill_kernel(FillParams p)
+{
+    const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= p.rows_total) return;
+    int64_t b = row / p.M;
+    const int m = (int)(row - b * p.M);
+    int64_t coff = 0, boff = 0;
+    for (int d = p.nbd - 1; d >= 0; --d) {
+        const int64_t i = b % p.bsize[d];
+        b /= p.bsize[d];
+        coff += i * p.c_bs[d];
+        boff += i * p.bias_bs[d];
+    }
+    float* c = p.C + coff + (int64_t)m * p.ldc;
+    const float* bi = p.bias ? p.bias + boff + (int64_t)m * p.bias_rs : nullptr;
+    auto val = [&](int n) {
+        float v = 0.f;
+        if (bi && (p.epi & mg::kEpiBias)) v += bi[(int64_t)n * p.bias_cs];
+        if ((p.epi & mg::kEpiCausal) && n > m) v = -INFINITY;
+        return v;
+    };
+    if (p.epi & mg::kEpiSoftmax) {
+        float mx = -INFINITY, sum = 0.f;
+        for (int n = 0; n < p.N; ++n) mx = fmaxf(mx, val(n));
+        for (int n = 0; n < p.N; ++n) sum += expf(val(n) - mx);
+        for (int n = 0; n < p.N; ++n) c[n] = expf(val(n) - mx) / sum;
+    } else {
+        for (int n = 0; n < p.N; ++n) c[n] = val(n) + (p.beta != 0.f ? p.beta * c[n] : 0.f);
+    }
+}
+
+// ---------------------------------------------------------------- workspace
+struct Workspace {
+    void* stream;
+    void* ptrs[2] = {nullptr, nullptr};
+    int n = 0;
+    ~Workspace()
+    {
+        for (int i = 0; i < n; ++i) {
+            if (g_free) g_free(ptrs[i], stream, g_alloc_ctx);
+            else cudaFreeAsync(ptrs[i], (cudaStream_t)stream);
+        }
+    }
+    void* get(size_t bytes)
+    {
+        void* p = nullptr;
+        if (g_alloc) p = g_alloc(bytes, stream, g_alloc_ctx);
+        else if (cudaMallocAsync(&p, bytes, (cudaStream_t)stream) != cudaSuccess) p = nullptr;
+        if (p) ptrs[n++] = p;
+        return p;
+    }
+};
+
+// Re-lays out operand x (stored rows x cols, per-dim batch strides) densely
+// with 16-byte row pitch; afterwards its batch strides are dense over its own
+// non-broadcast dims.
+mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace& ws, cudaStream_t st)
+{
+    PadParams pp;
+    pp.src = x.ptr;
+    pp.rows = x.rows;
+    pp.cols = x.cols;
+    pp.src_ld = x.ld;
+    pp.dst_ld = (x.cols + 3) / 4 * 4;
+    pp.nd = 0;
+    int64_t nbatch = 1;
+    int dims[MG_MAX_BATCH_DIMS];
+    for (int d = 0; d < nbd; ++d) {
+        if (x.bs[d] != 0 && bsize[d] != 1) {
+            dims[pp.nd] = d;
+            pp.size[pp.nd] = bsize[d];
+            pp.sstride[pp.nd] = x.bs[d];
+            pp.nd++;
+            nbatch *= bsize[d];
+        }
+    }
+    const int64_t mat = pp.rows * pp.dst_ld;
+    float* dst = static_cast<float*>(ws.get((size_t)(nbatch * mat) * sizeof(float) + 16));
+    if (!dst) return fail(MG_ERR_ALLOC, "workspace allocation of %lld bytes failed",
+                          (long long)(nbatch * mat * 4));
+    pp.dst = dst;
+    if (nbatch * x.rows > 0) {
+        if (nbatch * x.rows >= (1ll << 31)) return fail(MG_ERR_UNSUPPORTED, "operand too large to re-lay out");
+        pad_copy_kernel<<<(unsigned)(nbatch * x.rows), 128, 0, st>>>(pp);
+        MG_CUDA_TRY(cudaGetLastError());
+        g_launches++;
+    }
+    // new dense batch strides over the operand's own dims
+    int64_t s = mat;
+    for (int i = pp.nd - 1; i >= 0; --i) {
+        x.bs[dims[i]] = s;
+        s *= pp.size[i];
+    }
+    x.ptr = dst;
+    x.ld = pp.dst_ld;
+    return MG_OK;
+}
+
+template <int BN>
+mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb,
+                    mg::GemmParams& gp, cudaStream_t st)
+{
+    using L = mg::Layout<BN>;
+    const int split = gp.split;
+    const size_t fixed = 1024 + sizeof(mg::SharedState) + 64;
+    const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);
+    int stages = (int)((size_t)(dev->max_smem - (int)fixed) / per_stage);
+    stages = std::min(stages, mg::kMaxStages);
+    if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
+    gp.stages = stages;
+    const size_t smem = fixed + per_stage * stages;
+    auto k = kernel_of<BN>();
+    const int slot = bn_slot(BN);
+    if (dev->attr_smem[slot] < smem) {
+        MG_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        dev->attr_smem[slot] = smem;
+    }
+    const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
+    k<<<grid, mg::kThreads, smem, st>>>(ma, mb, gp);
+    MG_CUDA_TRY(cudaGetLastError());
+    g_launches++;
+    return MG_OK;
+}
+
+mg_status validate(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias)
+{
+    if (!d) return fail(MG_ERR_INVALID, "descriptor is NULL");
+    if (d->M < 0 || d->N < 0 || d->K < 0) return fail(MG_ERR_INVALID, "negative M/N/K (%d, %d, %d)", d->M, d->N, d->K);
+    if (d->batch_rank < 0 || d->batch_rank > MG_MAX_BATCH_DIMS)
+        return fail(MG_ERR_INVALID, "batch_rank %d outside [0, %d]", d->batch_rank, MG_MAX_BATCH_DIMS);
+    for (int i = 0; i < d->batch_rank; ++i)
+        if (d->batch[i] < 0) return fail(MG_ERR_INVALID, "negative batch size at dim %d", i);
+    if (d->mode != MG_MODE_DEFAULT && d->mode != MG_MODE_TF32X3 && d->mode != MG_MODE_TF32)
+        return fail(MG_ERR_INVALID, "unknown mode %d", d->mode);
+    if (d->epilogue & ~(MG_EPI_BIAS | MG_EPI_CAUSAL | MG_EPI_SOFTMAX))
+        return fail(MG_ERR_INVALID, "unknown epilogue flags 0x%x", d->epilogue);
+    if ((d->epilogue & MG_EPI_CAUSAL) && !(d->epilogue & MG_EPI_SOFTMAX))
+        return fail(MG_ERR_INVALID, "MG_EPI_CAUSAL requires MG_EPI_SOFTMAX");
+    if ((d->epilogue & MG_EPI_SOFTMAX) && d->N > 256)
+        return fail(MG_ERR_UNSUPPORTED, "softmax epilogue needs N <= 256 (got %d)", d->N);
+    if ((d->epilogue & MG_EPI_SOFTMAX) && d->beta != 0.f)
+        return fail(MG_ERR_INVALID, "softmax epilogue does not accumulate (beta must be 0)");
+    if ((d->epilogue & MG_EPI_BIAS) && !bias) return fail(MG_ERR_INVALID, "MG_EPI_BIAS with NULL bias");
+    const int64_t a_cols = d->trans_a ? d->M : d->K;
+    const int64_t b_cols = d->trans_b ? d->K : d->N;
+    if (d->lda < std::max<int64_t>(1, a_cols) || d->ldb < std::max<int64_t>(1, b_cols) ||
+        d->ldc < std::max<int64_t>(1, d->N))
+        return fail(MG_ERR_INVALID, "leading dimension smaller than the row length");
+    int64_t total = (int64_t)d->M * d->N;
+    for (int i = 0; i < d->batch_rank; ++i) total *= d->batch[i];
+    if (total > 0) {
+        if (!C) return fail(MG_ERR_INVALID, "C is NULL");
+        if (d->K > 0 && (!A || !B)) return fail(MG_ERR_INVALID, "A or B is NULL");
+    }
+    return MG_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+void mg_gemm_desc_init(mg_gemm_desc* d, int32_t M, int32_t N, int32_t K, int32_t trans_a, int32_t trans_b)
+{
+    std::memset(d, 0, sizeof(*d));
+    d->M = M;
+    d->N = N;
+    d->K = K;
+    d->trans_a = trans_a != 0;
+    d->trans_b = trans_b != 0;
+    d->lda = std::max<int64_t>(1, trans_a ? M : K);
+    d->ldb = std::max<int64_t>(1, trans_b ? K : N);
+    d->ldc = std::max<int64_t>(1, N);
+    d->alpha = 1.f;
+    d->beta = 0.f;
+    d->mode = MG_MODE_DEFAULT;
+}
+
+mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias,
+                  void* stream)
+{
+    g_last_error.clear();
+    mg_status s = validate(d, C, A, B, bias);
+    if (s != MG_OK) return s;
+    cudaStream_t st = (cudaStream_t)stream;
+    int64_t nbatch = 1;
+    for (int i = 0; i < d->batch_rank; ++i) nbatch *= d->batch[i];
+    if (d->M == 0 || d->N == 0 || nbatch == 0) return MG_OK;
+
+    DeviceState* dev = nullptr;
+    s = device_state(&dev);
+    if (s != MG_OK) return s;
+
+    const int nbd = d->batch_rank;
+    const bool has_bias = (d->epilogue & MG_EPI_BIAS) != 0;
+
+    if (d->K == 0) {
+        FillParams fp;
+        std::memset(&fp, 0, sizeof(fp));
+        fp.M = d->M;
+        fp.N = d->N;
+        fp.nbd = nbd;
+        for (int i = 0; i < nbd; ++i) {
+            fp.bsize[i] = d->batch[i];
+            fp.c_bs[i] = d->c_batch_stride[i];
+            fp.bias_bs[i] = d->bias_batch_stride[i];
+        }
+        fp.C = C;
+        fp.ldc = d->ldc;
+        fp.bias = has_bias ? bias : nullptr;
+        fp.bias_rs = d->bias_rs;
+        fp.bias_cs = d->bias_cs;
+        fp.beta = d->beta;
+        fp.epi = d->epilogue;
+        fp.rows_total = nbatch * d->M;
+        k0_fill_kernel<<<(unsigned)((fp.rows_total + 127) / 128), 128, 0, st>>>(fp);
+        MG_CUDA_TRY(cudaGetLastError());
+        g_launches++;
+        return MG_OK;
+    }
+
+    const int32_t mode = d->mode == MG_MODE_DEFAULT ? resolve_default_mode() : d->mode;
+
+    Operand a{A, d->trans_a ? d->K : d->M, d->trans_a ? d->M : d->K, d->lda, {0}};
+    Operand b{B, d->trans_b ? d->N : d->K, d->trans_b ? d->K : d->N, d->ldb, {0}};
+    for (int i = 0; i < nbd; ++i) {
+        a.bs[i] = d->a_batch_stride[i];
+        b.bs[i] = d->b_batch_stride[i];
+    }
+
+    Workspace ws;
+    ws.stream = stream;
+    BatchMap am, bmp;
+    bool a_ok = build_batch_map(nbd, d->batch, a.bs, &am) && tma_compatible(a, am);
+    if (!a_ok) {
+        s = relayout_operand(a, nbd, d->batch, ws, st);
+        if (s != MG_OK) return s;
+        if (!build_batch_map(nbd, d->batch, a.bs, &am) || !tma_compatible(a, am))
+            return fail(MG_ERR_UNSUPPORTED, "operand A cannot be mapped for TMA");
+    }
+    bool b_ok = build_batch_map(nbd, d->batch, b.bs, &bmp) && tma_compatible(b, bmp);
+    if (!b_ok) {
+        s = relayout_operand(b, nbd, d->batch, ws, st);
+        if (s != MG_OK) return s;
+        if (!build_batch_map(nbd, d->batch, b.bs, &bmp) || !tma_compatible(b, bmp))
+            return fail(MG_ERR_UNSUPPORTED, "operand B cannot be mapped for TMA");
+    }
+
+    int bn = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
+    if (d->epilogue & MG_EPI_SOFTMAX) bn = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
+
+    const int a_mn = d->trans_a ? 1 : 0;   // A stored [K][M]: M contiguous
+    const int b_mn = d->trans_b ? 0 : 1;   // B stored [K][N]: N contiguous
+    CUtensorMap ma, mb;
+    s = encode_map(&ma, a, am, a_mn, mg::kBM);
+    if (s != MG_OK) return s;
+    s = encode_map(&mb, b, bmp, b_mn, (uint32_t)bn);
+    if (s != MG_OK) return s;
+
+    mg::GemmParams gp;
+    std::memset(&gp, 0, sizeof(gp));
+    gp.M = d->M;
+    gp.N = d->N;
+    gp.K = d->K;
+    gp.num_kb = (d->K + mg::kBK - 1) / mg::kBK;
+    gp.m_tiles = (d->M + mg::kBM - 1) / mg::kBM;
+    gp.n_tiles = (d->N + bn - 1) / bn;
+    gp.tiles_per_batch = gp.m_tiles * gp.n_tiles;
+    const int64_t total = nbatch * gp.tiles_per_batch;
+    if (total >= (1ll << 31)) return fail(MG_ERR_UNSUPPORTED, "too many output tiles (%lld)", (long long)total);
+    gp.total_tiles = (int)total;
+    gp.group_m = 16;
+    gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
+    gp.a_mn = a_mn;
+    gp.b_mn = b_mn;
+    gp.a_rank = 2 + am.nmap;
+    gp.b_rank = 2 + bmp.nmap;
+    gp.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+               ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(mg::kBM >> 4) << 24);
+    gp.nbd = nbd;
+    for (int i = 0; i < mg::kMaxBatchDims; ++i) {
+        gp.bsize[i] = i < nbd ? d->batch[i] : 1;
+        gp.a_map[i] = am.map[i];
+        gp.b_map[i] = bmp.map[i];
+        gp.a_mult[i] = am.mult[i];
+        gp.b_mult[i] = bmp.mult[i];
+        gp.c_bs[i] = i < nbd ? d->c_batch_stride[i] : 0;
+        gp.bias_bs[i] = i < nbd ? d->bias_batch_stride[i] : 0;
+    }
+    gp.C = C;
+    gp.ldc = d->ldc;
+    gp.bias = has_bias ? bias : nullptr;
+    gp.bias_rs = d->bias_rs;
+    gp.bias_cs = d->bias_cs;
+    gp.alpha = d->alpha;
+    gp.beta = d->beta;
+    gp.epi = d->epilogue;
+    gp.status = dev->status;
+
+    switch (bn) {
+    case 64: return launch_tc<64>(dev, ma, mb, gp, st);
+    case 128: return launch_tc<128>(dev, ma, mb, gp, st);
+    default: return launch_tc<256>(dev, ma, mb, gp, st);
+    }
+}
+
+// Shared by mg_matmul / mg_matmul_bias / mg_matmul_softmax: turns the
+// reference's rank-equalised contiguous shapes into a descriptor. Mirrors the
+// shape checks of Functional::matmul (tensor_ops.cpp:4559-4572, 4807-4818).
+static mg_status seam_desc(mg_gemm_desc* d, const int32_t* out_shape, const int32_t* A_shape,
+                           const int32_t* B_shape, const int32_t* bias_shape, int32_t rank,
+                           int32_t trans_a, int32_t trans_b)
+{
+    if (!out_shape || !A_shape || !B_shape) return fail(MG_ERR_INVALID, "shape pointer is NULL");
+    if (rank < 2) return fail(MG_ERR_INVALID, "rank %d < 2: shapes must be rank-equalised to >= 2", rank);
+    if (rank - 2 > MG_MAX_BATCH_DIMS)
+        return fail(MG_ERR_UNSUPPORTED, "rank %d has more than %d leading dims", rank, MG_MAX_BATCH_DIMS);
+    for (int i = 0; i < rank; ++i)
+        if (out_shape[i] < 0 || A_shape[i] < 0 || B_shape[i] < 0 || (bias_shape && bias_shape[i] < 0))
+            return fail(MG_ERR_INVALID, "negative dimension at %d", i);
+    const int32_t M = trans_a ? A_shape[rank - 1] : A_shape[rank - 2];
+    const int32_t K = trans_a ? A_shape[rank - 2] : A_shape[rank - 1];
+    const int32_t Kb = trans_b ? B_shape[rank - 1] : B_shape[rank - 2];
+    const int32_t N = trans_b ? B_shape[rank - 2] : B_shape[rank - 1];
+    if (K != Kb) return fail(MG_ERR_INVALID, "incompatible inner dimensions %d and %d", K, Kb);
+    if (out_shape[rank - 2] != M || out_shape[rank - 1] != N)
+        return fail(MG_ERR_INVALID, "out shape [.., %d, %d] does not match [.., %d, %d]",
+                    out_shape[rank - 2], out_shape[rank - 1], M, N);
+    mg_gemm_desc_init(d, M, N, K, trans_a, trans_b);
+    d->batch_rank = rank - 2;
+    // contiguous element strides of each stored tensor; size-1 dims broadcast
+    int64_t sa = (int64_t)A_shape[rank - 2] * A_shape[rank - 1];
+    int64_t sb = (int64_t)B_shape[rank - 2] * B_shape[rank - 1];
+    int64_t sc = (int64_t)M * N;
+    int64_t sbias = bias_shape ? (int64_t)bias_shape[rank - 2] * bias_shape[rank - 1] : 0;
+    for (int i = rank - 3; i >= 0; --i) {
+        const int j = i;
+        if (!(A_shape[i] == B_shape[i] || A_shape[i] == 1 || B_shape[i] == 1))
+            return fail(MG_ERR_INVALID, "leading dim %d not broadcastable (%d vs %d)", i, A_shape[i], B_shape[i]);
+        const int32_t o = std::max(A_shape[i], B_shape[i]);
+        if (out_shape[i] != o) return fail(MG_ERR_INVALID, "out leading dim %d is %d, expected %d", i, out_shape[i], o);
+        d->batch[j] = o;
+        d->a_batch_stride[j] = A_shape[i] == 1 ? 0 : sa;
+        d->b_batch_stride[j] = B_shape[i] == 1 ? 0 : sb;
+        d->c_batch_stride[j] = out_shape[i] == 1 ? 0 : sc;
+        sa *= A_shape[i];
+        sb *= B_shape[i];
+        sc *= out_shape[i];
+        if (bias_shape) {
+            if (!(bias_shape[i] == o || bias_shape[i] == 1))
+                return fail(MG_ERR_INVALID, "bias dim %d is %d, not %d or 1", i, bias_shape[i], o);
+            d->bias_batch_stride[j] = bias_shape[i] == 1 ? 0 : sbias;
+            sbias *= bias_shape[i];
+        }
+    }
+    if (bias_shape) {
+        if (!(bias_shape[rank - 2] == M || bias_shape[rank - 2] == 1) ||
+            !(bias_shape[rank - 1] == N || bias_shape[rank - 1] == 1))
+            return fail(MG_ERR_INVALID, "bias [.., %d, %d] does not broadcast to [.., %d, %d]",
+                        bias_shape[rank - 2], bias_shape[rank - 1], M, N);
+        d->bias_rs = bias_shape[rank - 2] == 1 ? 0 : bias_shape[rank - 1];
+        d->bias_cs = bias_shape[rank - 1] == 1 ? 0 : 1;
+    }
+    return MG_OK;
+}
+
+mg_status mg_matmul(float* out, const float* A, const float* B, const int32_t* out_shape,
+                    const int32_t* A_shape, const int32_t* B_shape, int32_t rank, int32_t trans_a,
+                    int32_t trans_b, void* stream)
+{
+    g_last_error.clear();
+    mg_gemm_desc d;
+    mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, nullptr, rank, trans_a, trans_b);
+    if (s != MG_OK) return s;
+    return mg_gemm(&d, out, A, B, nullptr, stream);
+}
+
+mg_status mg_matmul_bias(float* out, const float* A, const float* B, const float* bias,
+                         const int32_t* out_shape, const int32_t* A_shape, const int32_t* B_shape,
+                         const int32_t* bias_shape, int32_t rank, int32_t trans_a, int32_t trans_b,
+                         void* stream)
+{
+    g_last_error.clear();
+    if (!bias_shape) return fail(MG_ERR_INVALID, "bias_shape is NULL");
+    mg_gemm_desc d;
+    mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, bias_shape, rank, trans_a, trans_b);
+    if (s != MG_OK) return s;
+    d.epilogue = MG_EPI_BIAS;
+    return mg_gemm(&d, out, A, B, bias, stream);
+}
+
+mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const float* bias,
+                            const int32_t* out_shape, const int32_t* A_shape, const int32_t* B_shape,
+                            const int32_t* bias_shape, int32_t rank, int32_t trans_a, int32_t trans_b,
+                            float alpha, int32_t causal, void* stream)
+{
+    g_last_error.clear();
+    mg_gemm_desc d;
+    mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, bias ? bias_shape : nullptr, rank,
+                            trans_a, trans_b);
+    if (s != MG_OK) return s;
+    if (bias && !bias_shape) return fail(MG_ERR_INVALID, "bias_shape is NULL");
+    d.alpha = alpha;
+    d.epilogue = MG_EPI_SOFTMAX | (bias ? MG_EPI_BIAS : 0) | (causal ? MG_EPI_CAUSAL : 0);
+    return mg_gemm(&d, out, A, B, bias, stream);
+}
+
+void mg_set_allocator(mg_alloc_fn alloc_fn, mg_free_fn free_fn, void* ctx)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (alloc_fn && free_fn) {
+        g_alloc = alloc_fn;
+        g_free = free_fn;
+        g_alloc_ctx = ctx;
+    } else {
+        g_alloc = nullptr;
+        g_free = nullptr;
+        g_alloc_ctx = nullptr;
+    }
+}
+
+mg_status mg_set_mode(int32_t mode)
+{
+    if (mode != MG_MODE_TF32X3 && mode != MG_MODE_TF32) return fail(MG_ERR_INVALID, "unknown mode %d", mode);
+    g_mode.store(mode);
+    return MG_OK;
+}
+
+int32_t mg_get_mode(void) { return resolve_default_mode(); }
+
+const char* mg_last_error(void) { return g_last_error.c_str(); }
+
+mg_status mg_device_status(int32_t* detail, int32_t reset)
+{
+    DeviceState* dev = nullptr;
+    mg_status s = device_state(&dev);
+    if (s != MG_OK) return s;
+    MG_CUDA_TRY(cudaDeviceSynchronize());
+    int h[2] = {0, 0};
+    MG_CUDA_TRY(cudaMemcpyFromSymbol(h, g_device_status, sizeof(h)));
+    if (detail) *detail = h[1];
+    if (reset) {
+        int z[2] = {0, 0};
+        MG_CUDA_TRY(cudaMemcpyToSymbol(g_device_status, z, sizeof(z)));
+    }
+    return (mg_status)h[0];
+}
+
+uint64_t mg_launch_count(void) { return g_launches.load(); }
+
+const char* mg_version(void) { return "mg_gemm 0.1.0 (sm_100a tcgen05 tf32 / 3xtf32)"; }
+
+}  // extern "C"

@@ -1,0 +1,240 @@
+"""Host-side mirror of Macrograd's matmul API over the sm_100a library.
+
+Mirrors, for torch CUDA tensors (device memory and streams only; no torch
+arithmetic on the product path):
+  matmul(mat0, mat1, transA, transB)            Functional::matmul
+      macrograd/source/tensor_ops.cpp:4482-4694
+  matmul(mat0, mat1, bias, transA, transB)      Functional::matmul with bias
+      macrograd/source/tensor_ops.cpp:4700-4949
+  matmul_backward(...)                          MatMulOp / MatMulBiasOp::_backward
+      macrograd/source/tensor_ops.cpp:4504-4517, 4723-4737
+  attention_scores(...)                         matmul(Q/sqrt(d), K, mask, false, true)
+      followed by softmax(-1), mini_shakespeare/include/transformer.h:233-234
+
+Shape rules, error conditions and messages follow the reference; the GEMM
+itself always runs in libmg_gemm.so (mg_matmul / mg_matmul_bias / mg_gemm).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from ._lib import MacrogradError, check, i32_array
+
+
+# ------------------------------------------------------------------ shapes
+def equalize(a_shape: Sequence[int], b_shape: Sequence[int], transA: bool, transB: bool):
+    """Rank-equalised storage shapes and the output shape, with the reference's
+    checks (tensor_ops.cpp:4521-4579). Returns (A, B, out, a_was_1d, b_was_1d)."""
+    a, b = list(a_shape), list(b_shape)
+    if len(a) == 0 or len(b) == 0:
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             "Trying to matrix multiply two tensors while a tensor is empty.")
+    if transA and len(a) < 2:
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             "Addint a transposition to a single dimensional tensor for a matmul call is not allowed.")
+    if transB and len(b) < 2:
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             "Addint a transposition to a single dimensional tensor for a matmul call is not allowed.")
+    a_was_1d, b_was_1d = len(a) == 1, len(b) == 1
+    if a_was_1d:
+        a = [1] + a
+    if b_was_1d:
+        b = b + [1]
+    while len(a) > len(b):
+        b = [1] + b
+    while len(b) > len(a):
+        a = [1] + a
+    ka = a[-2] if transA else a[-1]
+    kb = b[-1] if transB else b[-2]
+    if ka != kb:
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             "Incompatible dimensions found inside a matmul() call.\n"
+                             f"Matrix0 shape: {tuple(a_shape)} | Matrix1 shape: {tuple(b_shape)}")
+    for i in range(len(a) - 2):
+        if not (a[i] == b[i] or a[i] == 1 or b[i] == 1):
+            raise MacrogradError(_lib.MG_ERR_INVALID,
+                                 "Trying to matrix multiply two tensors with incompatible shapes.\n"
+                                 f"Found shapes | Unsqueezed Matrix0: {tuple(a)} | Unsqueezed Matrix1: {tuple(b)}")
+    out = [max(x, y) for x, y in zip(a[:-2], b[:-2])]
+    out += [a[-1] if transA else a[-2], b[-2] if transB else b[-1]]
+    return a, b, out, a_was_1d, b_was_1d
+
+
+def equalize_bias(bias_shape: Sequence[int], out_shape: Sequence[int]):
+    """Bias rank-equalised to the output (tensor_ops.cpp:4784-4785, 4807-4818)."""
+    bs = list(bias_shape)
+    if len(bs) > len(out_shape):
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             "Trying to add a bias to a matmul tensor with more dimensions than the matmul output.")
+    while len(bs) < len(out_shape):
+        bs = [1] + bs
+    for o, x in zip(out_shape, bs):
+        if not (o == x or x == 1):
+            raise MacrogradError(_lib.MG_ERR_INVALID,
+                                 "Trying to add a bias to a matmul tensor with incompatible shapes.\n"
+                                 f"Found shapes | Matmul output: {tuple(out_shape)} | Unsqueezed bias: {tuple(bs)}")
+    return bs
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _stream_handle(t: torch.Tensor, stream: Optional[torch.cuda.Stream]):
+    s = stream if stream is not None else torch.cuda.current_stream(t.device)
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _check_operand(t: torch.Tensor, name: str):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must be a CUDA tensor")
+    if t.dtype != torch.float32:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must be float32")
+    if not t.is_contiguous():
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must be contiguous (Macrograd tensors always are)")
+
+
+# ------------------------------------------------------------------ forward
+def matmul(mat0: torch.Tensor, mat1: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           transA: bool = False, transB: bool = False, out: Optional[torch.Tensor] = None,
+           stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Functional::matmul(mat0, mat1[, bias], transA, transB) on CUDA tensors."""
+    lib = _lib.load()
+    _check_operand(mat0, "mat0")
+    _check_operand(mat1, "mat1")
+    if bias is not None:
+        _check_operand(bias, "bias")
+    a, b, oshape, a1d, b1d = equalize(mat0.shape, mat1.shape, transA, transB)
+    if out is None:
+        out = torch.empty(oshape, device=mat0.device, dtype=torch.float32)
+    elif list(out.shape) != oshape or not out.is_contiguous():
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"out must be a contiguous tensor of shape {oshape}")
+    rank = len(oshape)
+    st = _stream_handle(mat0, stream)
+    if bias is None:
+        check(lib.mg_matmul(_ptr(out), _ptr(mat0), _ptr(mat1), i32_array(oshape), i32_array(a),
+                            i32_array(b), rank, int(transA), int(transB), st))
+    else:
+        bs = equalize_bias(bias.shape, oshape)
+        check(lib.mg_matmul_bias(_ptr(out), _ptr(mat0), _ptr(mat1), _ptr(bias), i32_array(oshape),
+                                 i32_array(a), i32_array(b), i32_array(bs), rank, int(transA),
+                                 int(transB), st))
+    if a1d:
+        out = out.squeeze(-2)
+    if b1d:
+        out = out.squeeze(-1)
+    return out
+
+
+def attention_scores(q: torch.Tensor, k: torch.Tensor, scale: float, causal: bool = True,
+                     mask: Optional[torch.Tensor] = None,
+                     stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """P = softmax(scale * q @ k^T (+ mask) (+ causal -inf), dim=-1), one kernel.
+
+    The reference computes this as Functional::matmul(Q / sqrt(d), K, mask,
+    false, true) then Tensor::softmax(-1) (transformer.h:233-234); dividing Q by
+    a power of two and scaling the product by the same power are bit-identical."""
+    lib = _lib.load()
+    _check_operand(q, "q")
+    _check_operand(k, "k")
+    a, b, oshape, _, _ = equalize(q.shape, k.shape, False, True)
+    out = torch.empty(oshape, device=q.device, dtype=torch.float32)
+    bs = equalize_bias(mask.shape, oshape) if mask is not None else None
+    check(lib.mg_matmul_softmax(_ptr(out), _ptr(q), _ptr(k), _ptr(mask), i32_array(oshape),
+                                i32_array(a), i32_array(b), i32_array(bs) if bs else None,
+                                len(oshape), 0, 1, ctypes.c_float(scale), int(causal),
+                                _stream_handle(q, stream)))
+    return out
+
+
+# ------------------------------------------------------------------ backward
+def _fold_batch(x_shape, y_shape, out_target, tX, tY):
+    """When a gradient's target is broadcast over every leading dim while the
+    GEMM operands are batched, sum_b X_b^T Y_b is one GEMM with the batch
+    folded into K -- provided the two operands stack their batch along the
+    contracted rows (stored K-rows contiguous). Returns the 2-D storage shapes
+    or None."""
+    if len(out_target) <= 2 or any(d != 1 for d in out_target[:-2]):
+        return None
+    nb = 1
+    for d in x_shape[:-2]:
+        nb *= d
+    # only stackable when the contracted dim is the stored ROW dim of both
+    # operands: X stored [.., K, M] with tX, Y stored [.., K, N] without tY
+    if not tX or tY:
+        return None
+    if list(x_shape[:-2]) != list(y_shape[:-2]):
+        return None
+    return [nb * x_shape[-2], x_shape[-1]], [nb * y_shape[-2], y_shape[-1]]
+
+
+def _grad_gemm(X: torch.Tensor, Y: torch.Tensor, tX: bool, tY: bool, target_shape,
+               accumulate: Optional[torch.Tensor], stream) -> torch.Tensor:
+    """matmul(X, Y, tX, tY) reduced to target_shape (the `+=` of
+    tensor_ops.cpp:3345-3451), optionally accumulated into `accumulate`."""
+    folded = _fold_batch(list(X.shape), list(Y.shape), list(target_shape), tX, tY)
+    lib = _lib.load()
+    st = _stream_handle(X, stream)
+    if folded is not None:
+        xs, ys = folded
+        oshape = [xs[-1], ys[-1]]
+        dst = accumulate if accumulate is not None else torch.empty(target_shape, device=X.device)
+        d = _lib.GemmDesc()
+        lib.mg_gemm_desc_init(ctypes.byref(d), oshape[0], oshape[1], xs[0], 1, 0)
+        d.beta = 1.0 if accumulate is not None else 0.0
+        check(lib.mg_gemm(ctypes.byref(d), _ptr(dst), _ptr(X), _ptr(Y), None, st))
+        return dst
+    res = matmul(X, Y, None, tX, tY, stream=stream)
+    if list(res.shape) != list(target_shape):
+        # broadcast operand: reduce the batched temporary over its unit dims
+        dims = [i for i, (r, t) in enumerate(zip(res.shape, target_shape)) if t == 1 and r != 1]
+        res = res.sum(dim=dims, keepdim=True)
+    if accumulate is not None:
+        accumulate.add_(res)
+        return accumulate
+    return res
+
+
+def matmul_backward(A: torch.Tensor, B: torch.Tensor, dC: torch.Tensor, transA: bool = False,
+                    transB: bool = False, has_bias: bool = False,
+                    bias_shape: Optional[Sequence[int]] = None,
+                    need_a: bool = True, need_b: bool = True,
+                    grad_a: Optional[torch.Tensor] = None, grad_b: Optional[torch.Tensor] = None,
+                    stream: Optional[torch.cuda.Stream] = None
+                    ) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor], Optional[torch.Tensor]]:
+    """Gradients of C = op(A) op(B) (+ bias) for an upstream dC, exactly the GEMMs
+    MatMulOp::_backward issues (tensor_ops.cpp:4504-4517):
+        dA = transA ? matmul(B, dC, transB, true) : matmul(dC, B, false, !transB)
+        dB = transB ? matmul(dC, A, true, transA) : matmul(A, dC, !transA, false)
+    with A and B rank-equalised as the forward left them, then reduced to their
+    shapes like `internal_gradient() += ...`. A gradient whose operand was
+    broadcast over the batch (a weight) is one GEMM with the batch folded into
+    K instead of a batched temporary plus a reduction. grad_a / grad_b, when
+    given, are accumulated into (beta = 1) instead of freshly allocated."""
+    a, b, oshape, _, _ = equalize(A.shape, B.shape, transA, transB)
+    Av = A.reshape(a)
+    Bv = B.reshape(b)
+    dCv = dC.reshape(oshape)
+    dA = dB = dbias = None
+    if need_a:
+        if transA:
+            dA = _grad_gemm(Bv, dCv, transB, True, a, grad_a.reshape(a) if grad_a is not None else None, stream)
+        else:
+            dA = _grad_gemm(dCv, Bv, False, not transB, a, grad_a.reshape(a) if grad_a is not None else None, stream)
+        dA = dA.reshape(A.shape)
+    if need_b:
+        if transB:
+            dB = _grad_gemm(dCv, Av, True, transA, b, grad_b.reshape(b) if grad_b is not None else None, stream)
+        else:
+            dB = _grad_gemm(Av, dCv, not transA, False, b, grad_b.reshape(b) if grad_b is not None else None, stream)
+        dB = dB.reshape(B.shape)
+    if has_bias:
+        bs = equalize_bias(bias_shape, oshape)
+        dims = [i for i, (o, x) in enumerate(zip(oshape, bs)) if x == 1 and o != 1]
+        dbias = dCv.sum(dim=dims, keepdim=True) if dims else dCv.clone()
+        dbias = dbias.reshape(bias_shape)
+    return dA, dB, dbias

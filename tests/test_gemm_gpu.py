@@ -1,0 +1,337 @@
+"""Parity of the sm_100a kernels (through the C ABI) with the oracle.
+
+Tolerances (Frobenius-normalised relative error ||x - ref||_F / ||ref||_F):
+    3xTF32 (default mode) <= 1e-5      TF32 (fast mode) <= 2e-3
+At the full config sizes the oracle runs on row / column / head slices: rows
+of C depend only on the same rows of op(A) (and all of op(B)), so a slice of
+the oracle equals the same slice of the full product bit for bit.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle_bridge as ob
+
+torch = pytest.importorskip("torch")
+import macrograd_b200 as mg  # noqa: E402
+from macrograd_b200 import _lib, functional as F  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+TOL = {_lib.MG_MODE_TF32X3: 1e-5, _lib.MG_MODE_TF32: 2e-3}
+MODES = [_lib.MG_MODE_TF32X3, _lib.MG_MODE_TF32]
+GOLDEN = np.load(__import__("os").path.join(ob.ROOT, "tests", "golden", "matmul_golden.npz"))
+
+
+@pytest.fixture(autouse=True)
+def _mode_guard():
+    lib = mg.load()
+    old = lib.mg_get_mode()
+    yield
+    lib.mg_set_mode(old)
+
+
+def set_mode(m):
+    assert mg.load().mg_set_mode(m) == 0
+
+
+def cuda(x):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.detach().cpu().numpy()
+
+
+def gpu_matmul(A, B, ta=False, tb=False, bias=None):
+    return host(F.matmul(cuda(A), cuda(B), cuda(bias) if bias is not None else None, ta, tb))
+
+
+def assert_close(x, ref, mode, what=""):
+    assert x.shape == ref.shape, f"{what}: shape {x.shape} vs {ref.shape}"
+    assert np.all(np.isfinite(x)) == np.all(np.isfinite(ref)), f"{what}: non-finite mismatch"
+    e = ob.frob_rel_err(x, ref)
+    assert e <= TOL[mode], f"{what}: frobenius rel err {e:.3e} > {TOL[mode]:.0e} (max/rms {ob.max_rel_err(x, ref):.3e})"
+    return e
+
+
+def status_ok():
+    detail = ctypes.c_int32(0)
+    return mg.load().mg_device_status(ctypes.byref(detail), 1), detail.value
+
+
+# ---------------------------------------------------------------- basics
+def test_device_is_b200():
+    assert torch.cuda.get_device_capability() == (10, 0)
+
+
+def test_tf32_operand_rounding_is_pinned():
+    """What the TF32 path does to an fp32 operand's low mantissa bits: with
+    x = 1 + 2^-11 + 2^-12 and 1 * x, truncation gives 1, round-to-nearest
+    1 + 2^-10. The split mode is exact either way (hi has no low bits); this
+    records which one the hardware does."""
+    x = np.float32(1 + 2.0 ** -11 + 2.0 ** -12)
+    A = np.zeros((128, 8), np.float32)
+    A[0, 0] = x
+    B = np.zeros((8, 16), np.float32)
+    B[0, 0] = 1.0
+    set_mode(_lib.MG_MODE_TF32)
+    c = gpu_matmul(A, B)[0, 0]
+    assert c in (np.float32(1.0), np.float32(1 + 2.0 ** -10))
+    set_mode(_lib.MG_MODE_TF32X3)
+    assert gpu_matmul(A, B)[0, 0] == x
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("name", sorted({k.split("/")[1] for k in GOLDEN.files if k.startswith("fwd/")}))
+def test_forward_vs_reference_golden(name, mode):
+    set_mode(mode)
+    g = lambda k: GOLDEN[f"fwd/{name}/{k}"]
+    ta, tb = (bool(x) for x in g("flags"))
+    bias = GOLDEN[f"fwd/{name}/bias"] if f"fwd/{name}/bias" in GOLDEN.files else None
+    assert_close(gpu_matmul(g("A"), g("B"), ta, tb, bias), g("C"), mode, name)
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("name", sorted({k.split("/")[1] for k in GOLDEN.files if k.startswith("bwd/")}))
+def test_backward_vs_reference_golden(name, mode):
+    set_mode(mode)
+    g = lambda k: GOLDEN[f"bwd/{name}/{k}"]
+    ta, tb = (bool(x) for x in g("flags"))
+    has_bias = f"bwd/{name}/bias" in GOLDEN.files
+    dA, dB, db = F.matmul_backward(cuda(g("A")), cuda(g("B")), cuda(g("dC")), ta, tb, has_bias,
+                                   g("bias").shape if has_bias else None)
+    assert_close(host(dA), g("dA"), mode, name + " dA")
+    assert_close(host(dB), g("dB"), mode, name + " dB")
+    if has_bias:
+        assert_close(host(db), g("dbias"), mode, name + " dbias")
+
+
+def test_attention_golden_fused_softmax():
+    set_mode(_lib.MG_MODE_TF32X3)
+    P = host(F.attention_scores(cuda(GOLDEN["attn/Q"]), cuda(GOLDEN["attn/K"]), 0.5, causal=True))
+    assert_close(P, GOLDEN["attn/P"], _lib.MG_MODE_TF32X3, "attn P")
+    P2 = host(F.attention_scores(cuda(GOLDEN["attn/Q"]), cuda(GOLDEN["attn/K"]), 0.5, causal=False,
+                                 mask=cuda(GOLDEN["attn/mask"])))
+    assert_close(P2, GOLDEN["attn/P"], _lib.MG_MODE_TF32X3, "attn P (mask tensor)")
+
+
+# ---------------------------------------------------------------- shapes
+ODD = [1, 7, 17, 65, 129]
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(m, n, k) for m in ODD for n in ODD for k in ODD
+                                   if (m * 7 + n * 3 + k) % 4 == 0])
+def test_odd_shapes_all_layouts(M, N, K, ta, tb):
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform((K, M) if ta else (M, K), M * 1000 + K)
+    B = ob.seeded_uniform((N, K) if tb else (K, N), N * 1000 + K + 1)
+    assert_close(gpu_matmul(A, B, bool(ta), bool(tb)), ob.oracle_matmul(A, B, bool(ta), bool(tb)),
+                 _lib.MG_MODE_TF32X3, f"{M}x{N}x{K} t{ta}{tb}")
+
+
+@pytest.mark.parametrize("sa,sb,ta,tb", [
+    ((2, 3, 1, 40, 36), (1, 3, 5, 36, 20), False, False),   # 5-D, broadcast on both sides
+    ((6, 1, 48, 32), (6, 32, 70), False, False),
+    ((3, 33, 20), (1, 33, 44), True, False),                  # transposed A, broadcast B
+    ((4, 130, 66), (4, 70, 66), False, True),                 # odd N tail with transB
+    ((2, 2, 300, 260), (260, 257), False, False),             # N > 256: two n-tiles
+])
+@pytest.mark.parametrize("mode", MODES)
+def test_batched_broadcast_layouts(sa, sb, ta, tb, mode):
+    set_mode(mode)
+    A = ob.seeded_uniform(sa, 101)
+    B = ob.seeded_uniform(sb, 102)
+    assert_close(gpu_matmul(A, B, ta, tb), ob.oracle_matmul(A, B, ta, tb), mode, f"{sa}x{sb}")
+
+
+@pytest.mark.parametrize("bias_shape", [(40,), (1, 40), (30, 1), (30, 40), (3, 1, 40), (3, 30, 40)])
+def test_bias_broadcast_forms(bias_shape):
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform((3, 30, 50), 201)
+    B = ob.seeded_uniform((50, 40), 202)
+    bias = ob.seeded_uniform(bias_shape, 203)
+    assert_close(gpu_matmul(A, B, bias=bias), ob.oracle_matmul(A, B, bias=bias), _lib.MG_MODE_TF32X3,
+                 str(bias_shape))
+
+
+def test_unaligned_rows_take_the_relayout_path():
+    # vocab-65 logits: rows of 260 bytes are not 16-byte multiples (TMA rule)
+    set_mode(_lib.MG_MODE_TF32X3)
+    dC = ob.seeded_normal((512, 65), 301)
+    table = ob.seeded_uniform((65, 384), 302)
+    x = ob.seeded_uniform((512, 384), 303)
+    assert_close(gpu_matmul(dC, table), ob.oracle_matmul(dC, table), 0, "dx = dC table")
+    assert_close(gpu_matmul(dC, x, True, False), ob.oracle_matmul(dC, x, True, False), 0, "dtable")
+    assert_close(gpu_matmul(x, table, False, True), ob.oracle_matmul(x, table, False, True), 0, "logits")
+
+
+def test_vector_operands_squeeze_like_reference():
+    A = ob.seeded_uniform((5, 7), 401)
+    v = ob.seeded_uniform((7,), 402)
+    r = gpu_matmul(A, v)
+    assert r.shape == (5,)
+    assert_close(r, ob.oracle_matmul(A, v), 0, "gemv")
+    r = gpu_matmul(v, ob.seeded_uniform((7, 3), 403))
+    assert r.shape == (3,)
+
+
+def test_k_zero_gives_bias_or_zero():
+    A = np.zeros((3, 5, 0), np.float32)
+    B = np.zeros((0, 4), np.float32)
+    assert np.array_equal(gpu_matmul(A, B), np.zeros((3, 5, 4), np.float32))
+    bias = ob.seeded_uniform((4,), 7)
+    assert np.array_equal(gpu_matmul(A, B, bias=bias), np.broadcast_to(bias, (3, 5, 4)))
+
+
+def test_empty_outputs():
+    assert gpu_matmul(np.zeros((0, 5), np.float32), np.ones((5, 3), np.float32)).shape == (0, 3)
+    assert gpu_matmul(np.zeros((2, 0, 5), np.float32), np.ones((5, 3), np.float32)).shape == (2, 0, 3)
+
+
+def test_beta_accumulate_into_existing_gradient():
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform((4, 64, 48), 501)
+    W = ob.seeded_uniform((48, 80), 502)
+    dC = ob.seeded_normal((4, 64, 80), 503)
+    prev = ob.seeded_normal((48, 80), 504)
+    g = cuda(prev)
+    F.matmul_backward(cuda(A), cuda(W), cuda(dC), need_a=False, grad_b=g)
+    _, dW, _ = ob.oracle_matmul_backward(A, W, dC)
+    assert_close(host(g), prev + dW, 0, "grad += dW (beta = 1)")
+
+
+def test_nonfinite_inputs_propagate():
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform((128, 32), 601)
+    B = ob.seeded_uniform((32, 64), 602)
+    A[3, 5] = np.inf
+    A[9, 0] = np.nan
+    C = gpu_matmul(A, B)
+    R = ob.oracle_matmul(A, B)
+    assert np.array_equal(np.isnan(C), np.isnan(R))
+    assert np.array_equal(np.isinf(C), np.isinf(R))
+    fin = np.isfinite(R)
+    assert ob.frob_rel_err(C[fin], R[fin]) <= 1e-5
+
+
+def test_readme_known_answer_on_gpu():
+    from test_oracle import (README_FINAL_GRAD, README_FINAL_PARAMS, README_LOSSES,
+                             readme_least_squares)
+    set_mode(_lib.MG_MODE_TF32X3)
+    losses, params, grad = readme_least_squares(
+        lambda A, x: gpu_matmul(A, x),
+        lambda A, dC: gpu_matmul(A, dC.reshape(4, 1), True, False).reshape(4))
+    assert np.allclose(losses, README_LOSSES, atol=5e-5)
+    assert np.allclose(params, README_FINAL_PARAMS, atol=5e-5)
+    assert np.allclose(grad, README_FINAL_GRAD, atol=5e-5)
+
+
+# ---------------------------------------------------------------- configs
+@pytest.mark.parametrize("mode", MODES)
+def test_config1_forward_and_backward(mode):
+    """A[8,256,384] @ W[384,384], U(-1,1) seed 1; backward with dC = ones."""
+    set_mode(mode)
+    A = ob.seeded_uniform((8, 256, 384), 1)
+    W = ob.seeded_uniform((384, 384), 1001)
+    dC = np.ones((8, 256, 384), np.float32)
+    C = gpu_matmul(A, W)
+    assert_close(C, ob.oracle_matmul(A, W), mode, "cfg1 C")
+    dA, dW, _ = F.matmul_backward(cuda(A), cuda(W), cuda(dC))
+    rA, rW, _ = ob.oracle_matmul_backward(A, W, dC)
+    assert_close(host(dA), rA, mode, "cfg1 dA")
+    assert_close(host(dW), rW, mode, "cfg1 dW")
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_config2_linear_layer(mode):
+    """X[16384,384] @ W[1536,384]^T + b, Kaiming-uniform W and b (bound
+    1/sqrt(384)*sqrt(6)... as sqrt(6/384)), dY ~ N(0,1); checked on row and
+    column slices of the oracle."""
+    set_mode(mode)
+    bound = float(np.sqrt(6.0 / 384))
+    X = ob.seeded_uniform((16384, 384), 2)
+    W = ob.seeded_uniform((1536, 384), 1002, -bound, bound)
+    b = ob.seeded_uniform((1536,), 2002, -bound, bound)
+    dY = ob.seeded_normal((16384, 1536), 3002)
+    Xg, Wg, dYg = cuda(X), cuda(W), cuda(dY)
+    Y = host(F.matmul(Xg, Wg, cuda(b), False, True))
+    rows = slice(8000, 8192)
+    assert_close(Y[rows], ob.oracle_matmul(X[rows], W, False, True, b), mode, "cfg2 Y rows")
+    dX, dW, db = F.matmul_backward(Xg, Wg, dYg, False, True, True, (1536,))
+    assert_close(host(dX)[rows], ob.oracle_matmul(dY[rows], W), mode, "cfg2 dX rows")
+    cols = slice(96, 160)
+    rdW = ob.oracle_matmul(dY, np.ascontiguousarray(X[:, cols]), True, False)
+    assert_close(host(dW)[:, cols], rdW, mode, "cfg2 dW cols")
+    assert_close(host(db), ob.oracle_reduce_to(dY, [1, 1536]).reshape(1536), _lib.MG_MODE_TF32X3, "cfg2 db")
+
+
+def test_config3_attention_forward_and_backward():
+    """Q,K ~ N(0, 1/8), V ~ N(0,1) [64,6,256,64]; S = QK^T/8 + causal, P =
+    softmax(S) fused; O = P V; backward with dO ~ N(0,1) through both GEMMs.
+    The oracle runs on 3 of the 384 (batch, head) slices."""
+    set_mode(_lib.MG_MODE_TF32X3)
+    shp = (64, 6, 256, 64)
+    Q = ob.seeded_normal(shp, 3, 0.0, 0.125)
+    K = ob.seeded_normal(shp, 1003, 0.0, 0.125)
+    V = ob.seeded_normal(shp, 2003)
+    dO = ob.seeded_normal(shp, 4003)
+    Qg, Kg, Vg, dOg = cuda(Q), cuda(K), cuda(V), cuda(dO)
+    P = F.attention_scores(Qg, Kg, 0.125, causal=True)
+    O = F.matmul(P, Vg)
+    dP, dV, _ = F.matmul_backward(P, Vg, dOg)
+    Ph, Oh, dPh, dVh = host(P), host(O), host(dP), host(dV)
+    mask = ob.oracle_causal_mask(256)
+    for (bi, hi) in [(0, 0), (31, 4), (63, 5)]:
+        q, k, v, do = Q[bi, hi], K[bi, hi], V[bi, hi], dO[bi, hi]
+        S = ob.oracle_matmul(q * np.float32(0.125), k, False, True, mask)
+        Pr = ob.oracle_softmax_rows(S)
+        assert_close(Ph[bi, hi], Pr, 0, "cfg3 P")
+        assert_close(Oh[bi, hi], ob.oracle_matmul(Pr, v), 0, "cfg3 O")
+        rdP, rdV, _ = ob.oracle_matmul_backward(Pr, v, do)
+        assert_close(dPh[bi, hi], rdP, 0, "cfg3 dP")
+        assert_close(dVh[bi, hi], rdV, 0, "cfg3 dV")
+    # score-GEMM backward: dQs = dS K, dK = dS^T Qs
+    dS = ob.seeded_normal(shp[:3] + (256,), 5003)
+    Qs = cuda(Q * np.float32(0.125))
+    dQs, dK, _ = F.matmul_backward(Qs, Kg, cuda(dS), False, True)
+    dQh, dKh = host(dQs), host(dK)
+    for (bi, hi) in [(5, 1), (40, 3)]:
+        rQ, rK, _ = ob.oracle_matmul_backward(Q[bi, hi] * np.float32(0.125), K[bi, hi], dS[bi, hi], False, True)
+        assert_close(dQh[bi, hi], rQ, 0, "cfg3 dQs")
+        assert_close(dKh[bi, hi], rK, 0, "cfg3 dK")
+
+
+@pytest.mark.parametrize("mode", MODES)
+def test_config4_square_8192_row_slices(mode):
+    """A,B[8192,8192] ~ U(-1,1) seed 4; rows 0..31 and 4096..4127 of C against
+    the oracle on the same row slices (bit-identical to its full product)."""
+    set_mode(mode)
+    n = 8192
+    A = ob.seeded_uniform((n, n), 4)
+    B = ob.seeded_uniform((n, n), 1004)
+    C = F.matmul(cuda(A), cuda(B))
+    torch.cuda.synchronize()
+    for r0 in (0, 4096):
+        rows = slice(r0, r0 + 32)
+        got = C[rows].cpu().numpy()
+        assert_close(got, ob.oracle_matmul(A[rows], B), mode, f"cfg4 rows {r0}")
+        # and against exact (float64) arithmetic: the GPU is at least as close as the oracle
+        exact = A[rows].astype(np.float64) @ B.astype(np.float64)
+        if mode == _lib.MG_MODE_TF32X3:
+            assert ob.frob_rel_err(got, exact) <= 1e-5
+
+
+def test_no_kernel_timed_out():
+    st, detail = status_ok()
+    assert st == 0, f"device status {st}, wait site {detail}"
+
+
+def test_native_launches_counted():
+    lib = mg.load()
+    before = lib.mg_launch_count()
+    gpu_matmul(np.ones((4, 4), np.float32), np.ones((4, 4), np.float32))
+    assert lib.mg_launch_count() == before + 1

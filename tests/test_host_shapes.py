@@ -1,0 +1,40 @@
+"""Host mirror of Functional::matmul's shape logic (no GPU needed)."""
+import pytest
+
+from macrograd_b200 import functional as F
+from macrograd_b200._lib import MacrogradError
+
+
+@pytest.mark.parametrize("a,b,ta,tb,out", [
+    ((8, 256, 384), (384, 384), False, False, [8, 256, 384]),
+    ((16384, 384), (1536, 384), False, True, [16384, 1536]),
+    ((64, 6, 256, 64), (64, 6, 256, 64), False, True, [64, 6, 256, 256]),
+    ((4, 4), (4,), False, False, [4, 1]),
+    ((7,), (7, 3), False, False, [1, 3]),
+    ((2, 1, 8, 10), (1, 3, 12, 8), True, True, [2, 3, 10, 12]),
+])
+def test_equalize_matches_reference_rules(a, b, ta, tb, out):
+    _, _, o, _, _ = F.equalize(a, b, ta, tb)
+    assert o == out
+
+
+@pytest.mark.parametrize("a,b,ta,tb", [((3, 4), (5, 6), False, False), ((4,), (4, 3), True, False),
+                                       ((2, 3, 4), (3, 4, 5), False, False)])
+def test_equalize_rejects_like_reference(a, b, ta, tb):
+    with pytest.raises(MacrogradError):
+        F.equalize(a, b, ta, tb)
+
+
+def test_bias_equalize():
+    assert F.equalize_bias((1536,), [16384, 1536]) == [1, 1536]
+    assert F.equalize_bias((256, 256), [64, 6, 256, 256]) == [1, 1, 256, 256]
+    with pytest.raises(MacrogradError):
+        F.equalize_bias((3,), [4, 5])
+
+
+def test_fold_batch_for_broadcast_weight_gradient():
+    # dW of A[8,256,384] @ W[384,384]: matmul(A, dC, true, false) summed over the batch
+    assert F._fold_batch([8, 256, 384], [8, 256, 384], [1, 384, 384], True, False) == \
+        ([2048, 384], [2048, 384])
+    assert F._fold_batch([8, 256, 384], [8, 256, 384], [8, 384, 384], True, False) is None
+    assert F._fold_batch([8, 384, 256], [8, 256, 384], [1, 384, 384], False, False) is None
