@@ -194,9 +194,12 @@ mg_status encode_map(CUtensorMap* map, const Operand& x, const BatchMap& bm, int
     }
     box[0] = 32;
     box[1] = box_rows_is_k ? 32u : box_outer;
+    // K-major boxes: 16-byte-chunk 128B swizzle; MN-major boxes: 32-byte-chunk
+    // 128B swizzle (the only MN-major layout the TF32 MMA reads).
+    const CUtensorMapSwizzle sw = box_rows_is_k ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
                           const_cast<float*>(x.ptr), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MG_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
     return MG_OK;

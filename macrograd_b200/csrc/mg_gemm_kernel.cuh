@@ -3,27 +3,36 @@
 // Computes, per output tile of 128 x BN, C = alpha * op(A) op(B) (+ bias)
 // (+ beta * C) or a fused row softmax of it, on fp32 operands through the TF32
 // tensor cores: one product per term (TF32 mode), or the 3xTF32 split
-// hi*hi + hi*lo + lo*hi (fp32-accurate mode; hi = x with its 13 low mantissa
-// bits cleared, lo = x - hi, which is exact in fp32).
+// hi*hi + hi*lo + lo*hi (fp32-accurate mode).
 //
-// Roles (320 threads, one CTA per SM):
-//   warps 0-3  epilogue: TMEM -> registers -> bias / scale / softmax -> HBM;
-//              warp w reads TMEM lanes 32w..32w+31 = tile rows 32w..32w+31.
-//   warps 4-7  split: on each landed stage, write lo tiles and clear the low
-//              bits of the raw tiles in place (3xTF32 mode only).
-//   warp 8     TMA producer (one lane): A and B tiles, 32 K-elements deep,
-//              128-byte swizzled, into a ring of STAGES stages.
-//   warp 9     TMEM allocator; one lane issues tcgen05.mma into one of two
-//              TMEM accumulators (double-buffered so the epilogue of tile i
-//              overlaps the main loop of tile i+1).
+// Two hardware facts shape the fp32-accurate mode (both pinned by GPU tests):
+//  * a TF32 MMA reads an fp32 operand truncated to its top 19 bits, so the raw
+//    tile already is `hi` and only lo = x - hi (exact in fp32) is written;
+//  * the MMA's accumulate into TMEM truncates, so the error of one accumulator
+//    grows with the number of MMAs added into it. The main loop therefore
+//    accumulates at most kChunkKb K-blocks (256 K-elements) into a TMEM
+//    *partial*, which the epilogue warps add into a TMEM *master* with fp32
+//    round-to-nearest adds; the error then no longer grows with K.
+//
+// Roles (448 threads = 14 warps, one CTA per SM):
+//   warps 0-7   epilogue: warp w owns TMEM lanes 32(w%4).. (tile rows) and the
+//               column half w/4. Per chunk: master (+)= partial. Per tile:
+//               alpha / bias / beta / store from the master; the row softmax
+//               runs in warps 0-3 with one thread per full row.
+//   warps 8-11  split (3xTF32 only): lo tile of every landed stage.
+//   warp 12     TMA producer (one lane).
+//   warp 13     TMEM allocator; one lane issues tcgen05.mma.
+// TMEM: columns [0, BN) partial, [BN, 2BN) master.
 //
 // Operand layouts in shared memory (per stage, 1024-byte aligned):
 //   K-major tile (op(X) rows contiguous in K): R rows x 128 B, one TMA box
-//     {32, R}; descriptor LBO 16 B, SBO 1024 B; +32 B per 8-deep K step.
+//     {32, R}, 128-byte swizzle of 16-byte chunks; descriptor LBO 16 B,
+//     SBO 1024 B; +32 B per 8-deep K step.
 //   MN-major tile (X stored with M or N contiguous, i.e. the transposed views
 //     the backward pass produces): R/32 boxes {32 (MN), 32 (K)} of 4 KB at
-//     4 KB spacing; descriptor LBO 4096 B (next 32 MN), SBO 1024 B (next 8 K);
-//     +1024 B per 8-deep K step.
+//     4 KB spacing, 128-byte rows swizzled in 32-byte chunks; descriptor
+//     LBO 4096 B (next 32 MN), SBO 512 B (next 4 K rows); +1024 B per 8-deep
+//     K step.
 // Transposed views are therefore read in place; nothing is materialised.
 //
 // Every wait is bounded (global timer). On expiry the kernel records
@@ -39,11 +48,18 @@ namespace mg {
 
 constexpr int kBM = 128;            // tile rows (MMA M)
 constexpr int kBK = 32;             // K elements per stage (128 bytes of fp32)
+constexpr int kChunkKb = 8;         // K-blocks accumulated in TMEM before promotion
 constexpr int kMaxStages = 8;
-constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kEpiThreads = kEpiWarps * 32;
+constexpr int kSplitWarp0 = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
+constexpr int kThreads = 14 * 32;
 constexpr int kMaxBatchDims = 6;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
+constexpr uint32_t kSleepHintNs = 20000u;          // try_wait suspend hint
 
 enum : int { kEpiBias = 1, kEpiCausal = 2, kEpiSoftmax = 4 };
 
@@ -51,10 +67,11 @@ enum : int { kEpiBias = 1, kEpiCausal = 2, kEpiSoftmax = 4 };
 enum : int {
     kWaitProducerEmpty = 1,
     kWaitSplitFull = 2,
-    kWaitMmaAccEmpty = 3,
+    kWaitMmaPartialFree = 3,
     kWaitMmaStage = 4,
-    kWaitEpilogueFull = 5,
-    kWaitDrain = 6
+    kWaitEpiloguePartial = 5,
+    kWaitEpilogueMaster = 6,
+    kWaitEpilogueMasterFree = 7
 };
 
 struct GemmParams {
@@ -121,8 +138,9 @@ struct SharedState {
     uint64_t full[kMaxStages];
     uint64_t split_done[kMaxStages];
     uint64_t empty[kMaxStages];
-    uint64_t acc_full[2];
-    uint64_t acc_empty[2];
+    uint64_t part_full;
+    uint64_t part_free;
+    uint64_t master_free;       // softmax mode: warps 0-3 finished reading a tile's master
     uint64_t drain;
     uint32_t tmem_base;
     volatile int abort_flag;
@@ -138,15 +156,20 @@ __device__ __forceinline__ void record_failure(const GemmParams& p, SharedState*
 
 // Bounded wait for the phase of parity `parity` of `bar`. Returns false when
 // the CTA is aborting (another role gave up) or this wait itself ran out.
+template <bool kSleep>
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, SharedState* ss,
                                            const GemmParams& p, int where)
 {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
+        if (kSleep) {
+            if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
+        } else {
 #pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_test(bar, parity)) return true;
+            for (int i = 0; i < 16; ++i)
+                if (mbar_test(bar, parity)) return true;
+        }
         if (ss->abort_flag) return false;
         if (global_timer_ns() - t0 > kWaitLimitNs) {
             record_failure(p, ss, where);
@@ -169,10 +192,9 @@ struct Layout {
     static constexpr uint32_t kABytes = kBM * 128;          // 16 KB
     static constexpr uint32_t kBBytes = BN * 128;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kTmemCols = 2 * BN;           // double-buffered accumulator
+    static constexpr uint32_t kTmemCols = 2 * BN;           // partial + master
 };
 
-template <int BN>
 __device__ __forceinline__ void store_row_chunk(float* crow, int gn0, int nvalid, const float* v)
 {
     if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(crow + gn0) & 15u) == 0)) {
@@ -216,19 +238,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&ss->split_done[s]), 128);
             mbar_init(smem_u32(&ss->empty[s]), 1);
         }
-        for (int a = 0; a < 2; ++a) {
-            mbar_init(smem_u32(&ss->acc_full[a]), 1);
-            mbar_init(smem_u32(&ss->acc_empty[a]), 128);
-        }
+        mbar_init(smem_u32(&ss->part_full), 1);
+        mbar_init(smem_u32(&ss->part_free), kEpiThreads);
+        mbar_init(smem_u32(&ss->master_free), kEpiThreads / 2);
         mbar_init(smem_u32(&ss->drain), 1);
         ss->abort_flag = 0;
         mbar_fence_init();
     }
-    if (warp == 8 && lane == 0) {
+    if (warp == kProducerWarp && lane == 0) {
         tma_prefetch_map(&tmA);
         tma_prefetch_map(&tmB);
     }
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tmem_alloc(smem_u32(&ss->tmem_base), L::kTmemCols);
         tmem_relinquish();
     }
@@ -237,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = ss->tmem_base;
 
-    if (warp == 8) {
+    if (warp == kProducerWarp) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             int stage = 0;
@@ -248,16 +269,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const TileCoord tc = decode_tile(t, p);
                 int idx[kMaxBatchDims];
                 batch_index(tc.batch, p, idx);
-                int32_t ca[5] = {0, 0, 0, 0, 0}, cb[5] = {0, 0, 0, 0, 0};
+                int32_t a2 = 0, a3 = 0, a4 = 0, b2 = 0, b3 = 0, b4 = 0;
 #pragma unroll
                 for (int d = 0; d < kMaxBatchDims; ++d) {
-                    if (d < p.nbd && p.a_map[d] >= 0) ca[2 + p.a_map[d]] += idx[d] * p.a_mult[d];
-                    if (d < p.nbd && p.b_map[d] >= 0) cb[2 + p.b_map[d]] += idx[d] * p.b_mult[d];
+                    if (d < p.nbd) {
+                        const int32_t va = idx[d] * p.a_mult[d];
+                        const int32_t vb = idx[d] * p.b_mult[d];
+                        a2 += p.a_map[d] == 0 ? va : 0;
+                        a3 += p.a_map[d] == 1 ? va : 0;
+                        a4 += p.a_map[d] == 2 ? va : 0;
+                        b2 += p.b_map[d] == 0 ? vb : 0;
+                        b3 += p.b_map[d] == 1 ? vb : 0;
+                        b4 += p.b_map[d] == 2 ? vb : 0;
+                    }
                 }
                 const int m0 = tc.mt * kBM;
                 const int n0 = tc.nt * BN;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!wait_phase(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
+                    if (!wait_phase<false>(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
                         ok = false;
                         break;
                     }
@@ -265,26 +294,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive_expect_tx(fb, L::kStageBytes);
                     const int k0 = kb * kBK;
                     if (!p.a_mn) {
-                        ca[0] = k0; ca[1] = m0;
-                        tma_load(&tmA, fb, a_raw(stage), p.a_rank, ca);
+                        tma_load(&tmA, fb, a_raw(stage), p.a_rank, k0, m0, a2, a3, a4);
                     } else {
-                        ca[1] = k0;
 #pragma unroll
-                        for (int j = 0; j < kBM / 32; ++j) {
-                            ca[0] = m0 + 32 * j;
-                            tma_load(&tmA, fb, a_raw(stage) + 4096u * j, p.a_rank, ca);
-                        }
+                        for (int j = 0; j < kBM / 32; ++j)
+                            tma_load(&tmA, fb, a_raw(stage) + 4096u * j, p.a_rank, m0 + 32 * j, k0, a2, a3, a4);
                     }
                     if (!p.b_mn) {
-                        cb[0] = k0; cb[1] = n0;
-                        tma_load(&tmB, fb, b_raw(stage), p.b_rank, cb);
+                        tma_load(&tmB, fb, b_raw(stage), p.b_rank, k0, n0, b2, b3, b4);
                     } else {
-                        cb[1] = k0;
 #pragma unroll
-                        for (int j = 0; j < BN / 32; ++j) {
-                            cb[0] = n0 + 32 * j;
-                            tma_load(&tmB, fb, b_raw(stage) + 4096u * j, p.b_rank, cb);
-                        }
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load(&tmB, fb, b_raw(stage) + 4096u * j, p.b_rank, n0 + 32 * j, k0, b2, b3, b4);
                     }
                     issued |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -298,41 +319,50 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp == 9) {
+    } else if (warp == kMmaWarp) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             const bool split = p.split != 0;
             const uint32_t a_lbo = p.a_mn ? 4096u : 16u;
             const uint32_t b_lbo = p.b_mn ? 4096u : 16u;
+            const uint32_t a_sbo = p.a_mn ? 512u : 1024u;
+            const uint32_t b_sbo = p.b_mn ? 512u : 1024u;
+            const uint32_t a_lay = p.a_mn ? kLayoutSw128Base32 : kLayoutSw128;
+            const uint32_t b_lay = p.b_mn ? kLayoutSw128Base32 : kLayoutSw128;
             const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
             const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
+            const uint32_t d_tmem = tmem_base;   // partial accumulator, columns [0, BN)
             int stage = 0;
             uint32_t phase = 0;
-            int acc = 0;
-            uint32_t acc_phase = 0;
+            uint32_t chunk_phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
-                if (!wait_phase(smem_u32(&ss->acc_empty[acc]), acc_phase ^ 1u, ss, p, kWaitMmaAccEmpty)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
+                    const bool chunk_start = (kb % kChunkKb) == 0;
+                    const bool chunk_end = (kb % kChunkKb) == kChunkKb - 1 || kb == p.num_kb - 1;
+                    if (chunk_start) {
+                        // the epilogue has taken the previous partial
+                        if (!wait_phase<false>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
+                                               kWaitMmaPartialFree)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
                     const uint32_t ready = split ? smem_u32(&ss->split_done[stage]) : smem_u32(&ss->full[stage]);
-                    if (!wait_phase(ready, phase, ss, p, kWaitMmaStage)) {
+                    if (!wait_phase<false>(ready, phase, ss, p, kWaitMmaStage)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
 #pragma unroll
                     for (int ks = 0; ks < kBK / 8; ++ks) {
-                        const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
-                        const uint64_t da = smem_desc_sw128(a_raw(stage) + ks * a_kstep, a_lbo, 1024u);
-                        const uint64_t db = smem_desc_sw128(b_raw(stage) + ks * b_kstep, b_lbo, 1024u);
+                        const uint32_t accum = (!chunk_start || ks > 0) ? 1u : 0u;
+                        const uint64_t da = smem_desc(a_raw(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
+                        const uint64_t db = smem_desc(b_raw(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                         if (split) {
-                            const uint64_t dal = smem_desc_sw128(a_lo(stage) + ks * a_kstep, a_lbo, 1024u);
-                            const uint64_t dbl = smem_desc_sw128(b_lo(stage) + ks * b_kstep, b_lbo, 1024u);
+                            const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
+                            const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                             tc_mma_tf32(d_tmem, dal, db, p.idesc, accum);   // lo * hi
                             tc_mma_tf32(d_tmem, da, dbl, p.idesc, 1u);      // hi * lo
                             tc_mma_tf32(d_tmem, da, db, p.idesc, 1u);       // hi * hi
@@ -342,48 +372,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_commit(smem_u32(&ss->empty[stage]));   // frees the stage when these MMAs finish
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
+                    if (chunk_end) {
+                        tc_commit(smem_u32(&ss->part_full)); // partial ready for promotion
+                        chunk_phase ^= 1u;
+                    }
                 }
-                if (!ok) break;
-                tc_commit(smem_u32(&ss->acc_full[acc]));      // accumulator ready for the epilogue
-                if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
             }
             // every MMA this thread issued has finished before TMEM is freed
             tc_commit(smem_u32(&ss->drain));
             drain_phase(smem_u32(&ss->drain), 0);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else if (warp >= kSplitWarp0) {
         // ------------------------------------------------ 3xTF32 split
         if (p.split) {
-            const int tid = threadIdx.x - 128;
+            const int tid = threadIdx.x - kSplitWarp0 * 32;
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!wait_phase(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)) {
+                    if (!wait_phase<true>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)) {
                         ok = false;
                         break;
                     }
-                    // A and B raw tiles are contiguous in the stage; their lo
-                    // tiles sit at the same offsets one raw region higher.
-                    uint4* raw = reinterpret_cast<uint4*>(smem + (size_t)stage * L::kStageBytes);
+                    // The MMA reads the raw tile as hi (the TF32 datapath drops the
+                    // 13 low mantissa bits); lo = x - hi is exact. Non-finite x
+                    // gets lo = 0 so it passes through hi alone.
+                    const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes);
                     uint4* lo = reinterpret_cast<uint4*>(smem + (size_t)stage * L::kStageBytes + raw_region);
                     constexpr int n4 = (int)(L::kStageBytes / 16);
 #pragma unroll 4
                     for (int i = tid; i < n4; i += 128) {
                         const uint4 x = raw[i];
-                        uint4 h, l;
-                        h.x = x.x & 0xFFFFE000u; h.y = x.y & 0xFFFFE000u;
-                        h.z = x.z & 0xFFFFE000u; h.w = x.w & 0xFFFFE000u;
-                        // lo = x - hi exactly; 0 for +-inf / nan so they pass through hi alone
-                        const float fx = __uint_as_float(x.x), fy = __uint_as_float(x.y);
-                        const float fz = __uint_as_float(x.z), fw = __uint_as_float(x.w);
-                        l.x = __float_as_uint(isfinite(fx) ? fx - __uint_as_float(h.x) : 0.f);
-                        l.y = __float_as_uint(isfinite(fy) ? fy - __uint_as_float(h.y) : 0.f);
-                        l.z = __float_as_uint(isfinite(fz) ? fz - __uint_as_float(h.z) : 0.f);
-                        l.w = __float_as_uint(isfinite(fw) ? fw - __uint_as_float(h.w) : 0.f);
-                        raw[i] = h;
+                        uint4 l;
+                        l.x = ((x.x & 0x7F800000u) == 0x7F800000u) ? 0u
+                              : __float_as_uint(__uint_as_float(x.x) - __uint_as_float(x.x & 0xFFFFE000u));
+                        l.y = ((x.y & 0x7F800000u) == 0x7F800000u) ? 0u
+                              : __float_as_uint(__uint_as_float(x.y) - __uint_as_float(x.y & 0xFFFFE000u));
+                        l.z = ((x.z & 0x7F800000u) == 0x7F800000u) ? 0u
+                              : __float_as_uint(__uint_as_float(x.z) - __uint_as_float(x.z & 0xFFFFE000u));
+                        l.w = ((x.w & 0x7F800000u) == 0x7F800000u) ? 0u
+                              : __float_as_uint(__uint_as_float(x.w) - __uint_as_float(x.w & 0xFFFFE000u));
                         lo[i] = l;
                     }
                     fence_proxy_async_smem();
@@ -393,13 +423,62 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ------------------------------------------------ epilogue (warps 0-3)
-        const int row = warp * 32 + lane;
-        int acc = 0;
-        uint32_t acc_phase = 0;
+        // ------------------------------------------------ epilogue (warps 0-7)
+        const int sub = warp & 3;                    // TMEM sub-partition = row group
+        const int half = warp >> 2;                  // column half
+        constexpr int kHalf = BN / 2;
+        const int row = sub * 32 + lane;
+        const uint32_t lane_base = tmem_base + ((uint32_t)(sub * 32) << 16);
+        const uint32_t t_part = lane_base + (uint32_t)(half * kHalf);
+        const uint32_t t_master = lane_base + (uint32_t)(BN + half * kHalf);
         const bool has_bias = (p.epi & kEpiBias) != 0;
-        for (int t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+        const bool softmax = (p.epi & kEpiSoftmax) != 0;
+        uint32_t chunk_phase = 0;
+        uint32_t mf_phase = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
             const TileCoord tc = decode_tile(t, p);
+            const int n_chunks = (p.num_kb + kChunkKb - 1) / kChunkKb;
+            if (softmax && half == 1) {
+                // warps 0-3 read the whole master row of the previous tile; do
+                // not overwrite this half before they are done with it
+                const bool freed = wait_phase<true>(smem_u32(&ss->master_free), mf_phase ^ 1u, ss, p,
+                                                    kWaitEpilogueMasterFree);
+                if (!__all_sync(0xffffffffu, freed)) break;
+                mf_phase ^= 1u;
+            }
+            // ---- promotions: master = sum of the tile's partials (fp32 round-to-nearest)
+            for (int c = 0; c < n_chunks; ++c) {
+                const bool got = wait_phase<true>(smem_u32(&ss->part_full), chunk_phase, ss, p, kWaitEpiloguePartial);
+                if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll 1
+                for (int j = 0; j < kHalf; j += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_part + j, r);
+                    if (c > 0) {
+                        uint32_t m[32];
+                        tmem_ld32(t_master + j, m);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            r[i] = __float_as_uint(__uint_as_float(m[i]) + __uint_as_float(r[i]));
+                    }
+                    tmem_st32(t_master + j, r);
+                }
+                tc_fence_before();
+                mbar_arrive(smem_u32(&ss->part_free));   // the MMA may overwrite the partial
+                chunk_phase ^= 1u;
+            }
+            if (!ok) break;
+            if (softmax) {
+                // all 256 epilogue threads have written their master columns
+                const bool synced = wait_phase<true>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
+                                                     kWaitEpilogueMaster);
+                if (!__all_sync(0xffffffffu, synced)) break;
+                tc_fence_after();
+            }
+
+            // ---- output epilogue from the master
             int idx[kMaxBatchDims];
             batch_index(tc.batch, p, idx);
             int64_t coff = 0, boff = 0;
@@ -416,68 +495,66 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool rok = gm < p.M;
             float* crow = p.C + coff + (int64_t)(rok ? gm : 0) * p.ldc;
             const float* brow = has_bias ? p.bias + boff + (int64_t)(rok ? gm : 0) * p.bias_rs : nullptr;
-
-            // every lane waits; the warp leaves together if any lane gave up, so
-            // the .sync.aligned TMEM loads below always run converged
-            const bool got = wait_phase(smem_u32(&ss->acc_full[acc]), acc_phase, ss, p, kWaitEpilogueFull);
-            if (!__all_sync(0xffffffffu, got)) break;
-            tc_fence_after();
-            const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * BN);
+            const uint32_t t_row = lane_base + (uint32_t)BN;   // master, column 0
 
             if (p.epi & kEpiSoftmax) {
-                // One thread owns one full row (N <= BN, single n-tile): the
-                // row softmax needs no cross-thread reduction.
-                const bool causal = (p.epi & kEpiCausal) != 0;
-                float mx = -INFINITY;
-                for (int c = 0; c < BN && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + c, r);
+                // Warps 0-3: one thread owns one full row (N <= BN, single
+                // n-tile), so the row softmax needs no cross-thread reduction.
+                if (half == 0) {
+                    const bool causal = (p.epi & kEpiCausal) != 0;
+                    float mx = -INFINITY;
+                    for (int c = 0; c < BN && c < p.N; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(t_row + c, r);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int gn = c + j;
-                        if (gn < p.N) {
-                            float v = p.alpha * __uint_as_float(r[j]);
-                            if (has_bias && rok) v += brow[(int64_t)gn * p.bias_cs];
-                            if (causal && gn > gm) v = -INFINITY;
-                            mx = fmaxf(mx, v);
+                        for (int j = 0; j < 32; ++j) {
+                            const int gn = c + j;
+                            if (gn < p.N) {
+                                float v = p.alpha * __uint_as_float(r[j]);
+                                if (has_bias && rok) v += brow[(int64_t)gn * p.bias_cs];
+                                if (causal && gn > gm) v = -INFINITY;
+                                mx = fmaxf(mx, v);
+                            }
                         }
                     }
-                }
-                float sum = 0.f;
-                for (int c = 0; c < BN && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + c, r);
+                    float sum = 0.f;
+                    for (int c = 0; c < BN && c < p.N; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(t_row + c, r);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int gn = c + j;
-                        if (gn < p.N) {
-                            float v = p.alpha * __uint_as_float(r[j]);
-                            if (has_bias && rok) v += brow[(int64_t)gn * p.bias_cs];
-                            if (causal && gn > gm) v = -INFINITY;
-                            sum += expf(v - mx);
+                        for (int j = 0; j < 32; ++j) {
+                            const int gn = c + j;
+                            if (gn < p.N) {
+                                float v = p.alpha * __uint_as_float(r[j]);
+                                if (has_bias && rok) v += brow[(int64_t)gn * p.bias_cs];
+                                if (causal && gn > gm) v = -INFINITY;
+                                sum += expf(v - mx);
+                            }
                         }
                     }
-                }
-                for (int c = 0; c < BN && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(taddr + c, r);
-                    float v[32];
+                    for (int c = 0; c < BN && c < p.N; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(t_row + c, r);
+                        float v[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int gn = c + j;
-                        float x = p.alpha * __uint_as_float(r[j]);
-                        if (gn < p.N && has_bias && rok) x += brow[(int64_t)gn * p.bias_cs];
-                        if (causal && gn > gm) x = -INFINITY;
-                        v[j] = expf(x - mx) / sum;
+                        for (int j = 0; j < 32; ++j) {
+                            const int gn = c + j;
+                            float x = p.alpha * __uint_as_float(r[j]);
+                            if (gn < p.N && has_bias && rok) x += brow[(int64_t)gn * p.bias_cs];
+                            if (causal && gn > gm) x = -INFINITY;
+                            v[j] = expf(x - mx) / sum;
+                        }
+                        if (rok) store_row_chunk(crow, c, min(32, p.N - c), v);
                     }
-                    if (rok) store_row_chunk<BN>(crow, c, min(32, p.N - c), v);
+                    tc_fence_before();
+                    mbar_arrive(smem_u32(&ss->master_free));
                 }
             } else {
-                for (int c = 0; c < BN; c += 32) {
+                for (int c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
                     const int gn0 = n0 + c;
                     if (gn0 >= p.N) break;   // uniform across the warp
                     uint32_t r[32];
-                    tmem_ld32(taddr + c, r);
+                    tmem_ld32(t_row + c, r);
                     if (rok) {
                         const int nvalid = min(32, p.N - gn0);
                         float v[32];
@@ -493,19 +570,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int j = 0; j < 32; ++j)
                                 if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
                         }
-                        store_row_chunk<BN>(crow, gn0, nvalid, v);
+                        store_row_chunk(crow, gn0, nvalid, v);
                     }
                 }
             }
             tc_fence_before();
-            mbar_arrive(smem_u32(&ss->acc_empty[acc]));
-            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem_base, L::kTmemCols);
     }

@@ -57,6 +57,22 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity)
     return ok != 0;
 }
 
+// As mbar_test, but the thread may sleep up to `hint_ns` waiting for the
+// phase (it wakes when the phase completes), so waiting warps do not take
+// issue slots from working warps on the same sub-partition.
+__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Generic-proxy writes to shared memory become visible to the async proxy
 // (tensor core operand reads, TMA).
 __device__ __forceinline__ void fence_proxy_async_smem()
@@ -71,9 +87,9 @@ __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map)
 }
 
 // Tiled tensor load of one box into shared memory, completing `bar`'s
-// transaction count. Coordinates innermost first.
-__device__ __forceinline__ void tma_load(const CUtensorMap* map, uint32_t bar, uint32_t dst,
-                                         int rank, const int32_t* c)
+// transaction count. Coordinates innermost first (c0 contiguous dim).
+__device__ __forceinline__ void tma_load(const CUtensorMap* map, uint32_t bar, uint32_t dst, int rank,
+                                         int32_t c0, int32_t c1, int32_t c2, int32_t c3, int32_t c4)
 {
     const uint64_t m = reinterpret_cast<uint64_t>(map);
     switch (rank) {
@@ -81,28 +97,28 @@ __device__ __forceinline__ void tma_load(const CUtensorMap* map, uint32_t bar, u
         asm volatile(
             "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
             " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
-            "l"(m), "r"(bar), "r"(c[0]), "r"(c[1])
+            "l"(m), "r"(bar), "r"(c0), "r"(c1)
             : "memory");
         break;
     case 3:
         asm volatile(
             "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
             " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-            "l"(m), "r"(bar), "r"(c[0]), "r"(c[1]), "r"(c[2])
+            "l"(m), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
             : "memory");
         break;
     case 4:
         asm volatile(
             "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
             " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
-            "l"(m), "r"(bar), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3])
+            "l"(m), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
             : "memory");
         break;
     default:
         asm volatile(
             "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes"
             " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-            "l"(m), "r"(bar), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(c[4])
+            "l"(m), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
             : "memory");
         break;
     }
@@ -176,13 +192,39 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32])
         : "memory");
 }
 
+// Store 32 consecutive 32-bit columns of this warp's 32 lanes (layout of
+// tmem_ld32), then wait for the store, so a following tmem_ld32 of the same
+// columns by this thread observes it.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+        "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading and
-// stride byte offsets (16-byte units), version 1 (bits 46-47), 128-byte swizzle
-// (layout type 2, bits 61-63). Tiles are 1024-byte aligned, so base offset 0.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo)
+// stride byte offsets (16-byte units), version 1 (bits 46-47) and the layout
+// type (bits 61-63). Tiles are 1024-byte aligned, so base offset 0.
+//   K-major operands:  layout 2, 128-byte swizzle of 16-byte chunks
+//                      (TMA CU_TENSOR_MAP_SWIZZLE_128B).
+//   MN-major operands: layout 1, 128-byte swizzle of 32-byte chunks, the only
+//                      MN-major layout TF32 operands accept
+//                      (TMA CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B).
+constexpr uint32_t kLayoutSw128 = 2;
+constexpr uint32_t kLayoutSw128Base32 = 1;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout)
 {
     return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
 }  // namespace mg

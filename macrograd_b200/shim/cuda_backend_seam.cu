@@ -1,0 +1,24 @@
+// cuda_backend_seam.cu -- the reference's CUDA backend with the matmul seam.
+//
+// Compiles the reference's macrograd/kernels/cuda_backend.cu UNMODIFIED, from
+// where it lies (include path set by the Makefile), with its two cuBLASLt
+// matmul entry points renamed out of the way by the preprocessor, and then
+// defines kernel_ops::matmul / matmul_bias from kernel_ops_matmul.inc in the
+// same translation unit (so the seam sees `stream`, MemPool and
+// MACROGRAD_CHECK exactly as the replaced code did). The renamed cuBLASLt
+// functions are dead code: nothing calls them.
+#define matmul mg_unused_cublaslt_matmul
+#define matmul_bias mg_unused_cublaslt_matmul_bias
+#include "cuda_backend.cu"
+#undef matmul
+#undef matmul_bias
+
+namespace kernel_ops {
+void matmul(void* out_data, const void* A_data, const void* B_data, const Shape& out_shape,
+            const Shape& A_shape, const Shape& B_shape, bool transA, bool transB);
+void matmul_bias(void* out_data, const void* A_data, const void* B_data, const void* bias,
+                 const Shape& out_shape, const Shape& A_shape, const Shape& B_shape,
+                 const Shape& bias_shape, bool transA, bool transB);
+}  // namespace kernel_ops
+
+#include "kernel_ops_matmul.inc"
