@@ -126,6 +126,33 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
                             int32_t rank, int32_t trans_a, int32_t trans_b,
                             float alpha, int32_t causal, void* stream);
 
+/* No counterpart in the reference: an allocation-free form of mg_matmul.
+ *
+ * Some callers cannot let a library allocate device memory during a call:
+ * runtimes that plan all device memory ahead of time and own every byte of
+ * it, or latency-critical loops that must not touch an allocator. mg_matmul
+ * itself allocates only in one case -- an operand whose row pitch is not a
+ * multiple of 16 bytes (e.g. rows of 65 floats) is first copied into padded
+ * scratch -- and this entry point takes that scratch from a fixed buffer
+ * inside the library instead: a file-scope device array of
+ * MG_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
+ * until the process exits. It calls no cudaMalloc / cudaFree and no
+ * allocator. Arguments, results and errors are those of mg_matmul.
+ *
+ * Limits: a call whose re-laid-out operands would need more than
+ * MG_NOALLOC_SCRATCH_BYTES is rejected with MG_ERR_INVALID before anything
+ * runs. The buffer is shared by all calls on a device and keeps the previous
+ * call's contents (every byte a call reads it has written first, so nothing
+ * needs clearing); calls that overlap on the GPU (several streams, or several
+ * host threads) race on it, so serialise them. The first call on each device
+ * looks up the buffer's device address; make that first call before any
+ * stream capture. */
+#define MG_NOALLOC_SCRATCH_BYTES (16u << 20)
+mg_status mg_matmul_noalloc(float* out, const float* A, const float* B,
+                            const int32_t* out_shape, const int32_t* A_shape,
+                            const int32_t* B_shape, int32_t rank, int32_t trans_a,
+                            int32_t trans_b, void* stream);
+
 /* Workspace allocator, stream-ordered like the reference's MemPool
  * (cuda_backend.h:63-79: cudaMallocAsync / cudaFreeAsync on the library
  * stream). The library asks for scratch only on paths that need it (operands

@@ -82,6 +82,7 @@ SIGNATURES = {
     "mg_matmul_bias": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
     "mg_matmul_softmax": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32P, _I32, _I32, _I32,
                                          ctypes.c_float, _I32, _P]),
+    "mg_matmul_noalloc": (ctypes.c_int, [_P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
     "mg_set_allocator": (None, [_P, _P, _P]),
     "mg_set_mode": (ctypes.c_int, [_I32]),
     "mg_get_mode": (ctypes.c_int32, []),

@@ -35,6 +35,12 @@ std::mutex g_mu;
 
 __device__ int g_device_status[2];
 
+// Fixed scratch of mg_matmul_noalloc (MG_NOALLOC_SCRATCH_BYTES), one copy per
+// GPU that loads this library, held until the process exits. In host code this
+// name is only a handle for cudaGetSymbolAddress, never a device address.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[MG_NOALLOC_SCRATCH_BYTES];
+uint8_t* g_noalloc_ptr[64] = {nullptr};   // its device address, per device ordinal
+
 constexpr int kMaxDevices = 64;
 struct DeviceState {
     bool ready = false;
@@ -280,12 +286,19 @@ __global__ void k0_fill_kernel(FillParams p)
 }
 
 // ---------------------------------------------------------------- workspace
+// Per-call scratch. By default it allocates through the registered allocator
+// (or cudaMallocAsync) and frees stream-ordered at the end of the call. Given
+// an arena (the no-allocation entry point), it hands out 256-byte aligned
+// pieces of that fixed buffer instead and never allocates or frees.
 struct Workspace {
     void* stream;
     void* ptrs[2] = {nullptr, nullptr};
     int n = 0;
+    uint8_t* arena = nullptr;
+    size_t arena_cap = 0, arena_used = 0;
     ~Workspace()
     {
+        if (arena) return;
         for (int i = 0; i < n; ++i) {
             if (g_free) g_free(ptrs[i], stream, g_alloc_ctx);
             else cudaFreeAsync(ptrs[i], (cudaStream_t)stream);
@@ -293,6 +306,12 @@ struct Workspace {
     }
     void* get(size_t bytes)
     {
+        if (arena) {
+            const size_t at = (arena_used + 255) & ~size_t(255);
+            if (at + bytes > arena_cap) return nullptr;
+            arena_used = at + bytes;
+            return arena + at;
+        }
         void* p = nullptr;
         if (g_alloc) p = g_alloc(bytes, stream, g_alloc_ctx);
         else if (cudaMallocAsync(&p, bytes, (cudaStream_t)stream) != cudaSuccess) p = nullptr;
@@ -300,6 +319,16 @@ struct Workspace {
         return p;
     }
 };
+
+// Scratch bytes relayout_operand asks for: the operand's distinct batch
+// elements, each rows x (cols rounded up to 4 floats), plus 16 bytes.
+size_t relayout_bytes(const Operand& x, int nbd, const int32_t* bsize)
+{
+    int64_t nbatch = 1;
+    for (int d = 0; d < nbd; ++d)
+        if (x.bs[d] != 0 && bsize[d] != 1) nbatch *= bsize[d];
+    return (size_t)(nbatch * x.rows * ((x.cols + 3) / 4 * 4)) * sizeof(float) + 16;
+}
 
 // Re-lays out operand x (stored rows x cols, per-dim batch strides) densely
 // with 16-byte row pitch; afterwards its batch strides are dense over its own
@@ -426,8 +455,11 @@ void mg_gemm_desc_init(mg_gemm_desc* d, int32_t M, int32_t N, int32_t K, int32_t
     d->mode = MG_MODE_DEFAULT;
 }
 
-mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias,
-                  void* stream)
+// The body of mg_gemm. With arena == nullptr the per-call scratch (operand
+// re-layout) is allocated as usual; with an arena it comes from that fixed
+// buffer and a request that does not fit is rejected before anything runs.
+static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, const float* B,
+                           const float* bias, void* stream, uint8_t* arena, size_t arena_cap)
 {
     g_last_error.clear();
     mg_status s = validate(d, C, A, B, bias);
@@ -480,15 +512,27 @@ mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* 
 
     Workspace ws;
     ws.stream = stream;
+    ws.arena = arena;
+    ws.arena_cap = arena_cap;
     BatchMap am, bmp;
-    bool a_ok = build_batch_map(nbd, d->batch, a.bs, &am) && tma_compatible(a, am);
+    const bool a_ok = build_batch_map(nbd, d->batch, a.bs, &am) && tma_compatible(a, am);
+    const bool b_ok = build_batch_map(nbd, d->batch, b.bs, &bmp) && tma_compatible(b, bmp);
+    if (arena) {
+        size_t need = 0;
+        if (!a_ok) need = ((need + 255) & ~size_t(255)) + relayout_bytes(a, nbd, d->batch);
+        if (!b_ok) need = ((need + 255) & ~size_t(255)) + relayout_bytes(b, nbd, d->batch);
+        if (need > arena_cap)
+            return fail(MG_ERR_INVALID,
+                        "this call needs %zu bytes of scratch to re-lay out its operands; the "
+                        "no-allocation entry point has %zu (MG_NOALLOC_SCRATCH_BYTES)",
+                        need, arena_cap);
+    }
     if (!a_ok) {
         s = relayout_operand(a, nbd, d->batch, ws, st);
         if (s != MG_OK) return s;
         if (!build_batch_map(nbd, d->batch, a.bs, &am) || !tma_compatible(a, am))
             return fail(MG_ERR_UNSUPPORTED, "operand A cannot be mapped for TMA");
     }
-    bool b_ok = build_batch_map(nbd, d->batch, b.bs, &bmp) && tma_compatible(b, bmp);
     if (!b_ok) {
         s = relayout_operand(b, nbd, d->batch, ws, st);
         if (s != MG_OK) return s;
@@ -552,6 +596,12 @@ mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* 
     case 128: return launch_tc<128>(dev, ma, mb, gp, st);
     default: return launch_tc<256>(dev, ma, mb, gp, st);
     }
+}
+
+mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias,
+                  void* stream)
+{
+    return gemm_impl(d, C, A, B, bias, stream, nullptr, 0);
 }
 
 // Shared by mg_matmul / mg_matmul_bias / mg_matmul_softmax: turns the
@@ -653,6 +703,33 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
     d.alpha = alpha;
     d.epilogue = MG_EPI_SOFTMAX | (bias ? MG_EPI_BIAS : 0) | (causal ? MG_EPI_CAUSAL : 0);
     return mg_gemm(&d, out, A, B, bias, stream);
+}
+
+// mg_matmul without any allocation: the only scratch it may need (the padded
+// copy of an operand whose rows break TMA's 16-byte rule) comes from
+// g_noalloc_scratch. Its device address is looked up on this entry point's
+// first call on each device (cudaGetSymbolAddress, with that device current)
+// and cached; that first call should therefore come before any stream capture.
+mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const int32_t* out_shape,
+                            const int32_t* A_shape, const int32_t* B_shape, int32_t rank,
+                            int32_t trans_a, int32_t trans_b, void* stream)
+{
+    g_last_error.clear();
+    mg_gemm_desc d;
+    mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, nullptr, rank, trans_a, trans_b);
+    if (s != MG_OK) return s;
+    int dev = 0;
+    MG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(MG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (g_noalloc_ptr[dev] == nullptr) {
+            void* p = nullptr;
+            MG_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+        }
+    }
+    return gemm_impl(&d, out, A, B, nullptr, stream, g_noalloc_ptr[dev], MG_NOALLOC_SCRATCH_BYTES);
 }
 
 void mg_set_allocator(mg_alloc_fn alloc_fn, mg_free_fn free_fn, void* ctx)
