@@ -46,7 +46,8 @@ struct DeviceState {
     bool ready = false;
     int sm_count = 0;
     int max_smem = 0;
-    size_t attr_smem[3] = {0, 0, 0};   // dynamic smem opted in, per tile width
+    size_t attr_smem[6] = {0, 0, 0, 0, 0, 0};   // dynamic smem opted in, per kernel variant
+    int max_clusters[3] = {0, 0, 0};            // resident CTA pairs, per pair-kernel tile width
     int* status = nullptr;   // device address of g_device_status
 };
 DeviceState g_dev[kMaxDevices];
@@ -84,10 +85,10 @@ int32_t resolve_default_mode()
     return g_mode.load();
 }
 
-template <int BN>
+template <int BN, bool kPair>
 constexpr auto kernel_of()
 {
-    return &mg::mg_gemm_tc_kernel<BN>;
+    return &mg::mg_gemm_tc_kernel<BN, kPair>;
 }
 
 int bn_slot(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : 2); }
@@ -375,11 +376,11 @@ mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace&
     return MG_OK;
 }
 
-template <int BN>
+template <int BN, bool kPair>
 mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb,
                     mg::GemmParams& gp, cudaStream_t st)
 {
-    using L = mg::Layout<BN>;
+    using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
     const size_t fixed = 1024 + sizeof(mg::SharedState) + 64;
     const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);
@@ -388,17 +389,53 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
     gp.stages = stages;
     const size_t smem = fixed + per_stage * stages;
-    auto k = kernel_of<BN>();
-    const int slot = bn_slot(BN);
+    auto k = kernel_of<BN, kPair>();
+    const int slot = bn_slot(BN) + (kPair ? 3 : 0);
     if (dev->attr_smem[slot] < smem) {
         MG_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         dev->attr_smem[slot] = smem;
     }
-    const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
-    k<<<grid, mg::kThreads, smem, st>>>(ma, mb, gp);
-    MG_CUDA_TRY(cudaGetLastError());
+    if (kPair) {
+        // one cluster of two CTAs (two SMs) per work unit, persistent over the
+        // tiles; as many clusters as can be resident at once
+        cudaLaunchConfig_t cfg = {};
+        cfg.blockDim = dim3(mg::kThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (dev->max_clusters[slot - 3] == 0) {
+            cfg.gridDim = dim3((unsigned)dev->sm_count, 1, 1);
+            int n = 0;
+            MG_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, k, &cfg));
+            dev->max_clusters[slot - 3] = std::max(1, std::min(n, dev->sm_count / 2));
+        }
+        const int pairs = std::max(1, std::min(gp.total_tiles, dev->max_clusters[slot - 3]));
+        cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
+        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, gp));
+    } else {
+        const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
+        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, gp);
+        MG_CUDA_TRY(cudaGetLastError());
+    }
     g_launches++;
     return MG_OK;
+}
+
+// Pair kernel (two SMs per 256-row tile) when a batch has more than 128 rows;
+// MG_GEMM_PAIR=0 / =1 forces the single-SM / pair kernel (tests, tuning).
+bool use_pair(int M)
+{
+    if (const char* e = std::getenv("MG_GEMM_PAIR")) {
+        if (e[0] == '0') return false;
+        if (e[0] == '1') return true;
+    }
+    return M > mg::kBM;
 }
 
 mg_status validate(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias)
@@ -540,15 +577,17 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
             return fail(MG_ERR_UNSUPPORTED, "operand B cannot be mapped for TMA");
     }
 
-    int bn = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
-    if (d->epilogue & MG_EPI_SOFTMAX) bn = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
+    const int bn = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
+    const bool pair = use_pair(d->M);
+    const int tile_rows = pair ? 2 * mg::kBM : mg::kBM;   // output rows per tile
+    const int b_rows = pair ? bn / 2 : bn;                // B rows (N) one CTA loads
 
     const int a_mn = d->trans_a ? 1 : 0;   // A stored [K][M]: M contiguous
     const int b_mn = d->trans_b ? 0 : 1;   // B stored [K][N]: N contiguous
     CUtensorMap ma, mb;
     s = encode_map(&ma, a, am, a_mn, mg::kBM);
     if (s != MG_OK) return s;
-    s = encode_map(&mb, b, bmp, b_mn, (uint32_t)bn);
+    s = encode_map(&mb, b, bmp, b_mn, (uint32_t)b_rows);
     if (s != MG_OK) return s;
 
     mg::GemmParams gp;
@@ -557,7 +596,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.N = d->N;
     gp.K = d->K;
     gp.num_kb = (d->K + mg::kBK - 1) / mg::kBK;
-    gp.m_tiles = (d->M + mg::kBM - 1) / mg::kBM;
+    gp.m_tiles = (d->M + tile_rows - 1) / tile_rows;
     gp.n_tiles = (d->N + bn - 1) / bn;
     gp.tiles_per_batch = gp.m_tiles * gp.n_tiles;
     const int64_t total = nbatch * gp.tiles_per_batch;
@@ -569,8 +608,9 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.b_mn = b_mn;
     gp.a_rank = 2 + am.nmap;
     gp.b_rank = 2 + bmp.nmap;
+    // instruction descriptor: D f32, A/B tf32, majors, N = bn, M = 128 (one SM) or 256 (pair)
     gp.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-               ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(mg::kBM >> 4) << 24);
+               ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(tile_rows >> 4) << 24);
     gp.nbd = nbd;
     for (int i = 0; i < mg::kMaxBatchDims; ++i) {
         gp.bsize[i] = i < nbd ? d->batch[i] : 1;
@@ -591,10 +631,17 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.epi = d->epilogue;
     gp.status = dev->status;
 
+    if (pair) {
+        switch (bn) {
+        case 64: return launch_tc<64, true>(dev, ma, mb, gp, st);
+        case 128: return launch_tc<128, true>(dev, ma, mb, gp, st);
+        default: return launch_tc<256, true>(dev, ma, mb, gp, st);
+        }
+    }
     switch (bn) {
-    case 64: return launch_tc<64>(dev, ma, mb, gp, st);
-    case 128: return launch_tc<128>(dev, ma, mb, gp, st);
-    default: return launch_tc<256>(dev, ma, mb, gp, st);
+    case 64: return launch_tc<64, false>(dev, ma, mb, gp, st);
+    case 128: return launch_tc<128, false>(dev, ma, mb, gp, st);
+    default: return launch_tc<256, false>(dev, ma, mb, gp, st);
     }
 }
 

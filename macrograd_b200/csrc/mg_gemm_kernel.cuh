@@ -1,9 +1,20 @@
 // mg_gemm_kernel.cuh -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
-// Computes, per output tile of 128 x BN, C = alpha * op(A) op(B) (+ bias)
-// (+ beta * C) or a fused row softmax of it, on fp32 operands through the TF32
-// tensor cores: one product per term (TF32 mode), or the 3xTF32 split
-// hi*hi + hi*lo + lo*hi (fp32-accurate mode).
+// Computes C = alpha * op(A) op(B) (+ bias) (+ beta * C), or a fused row
+// softmax of it, on fp32 operands through the TF32 tensor cores: one product
+// per term (TF32 mode), or the 3xTF32 split hi*hi + hi*lo + lo*hi
+// (fp32-accurate mode).
+//
+// Two variants of one template:
+//   kPair = false  one CTA per SM, output tile 128 x BN, MMA M=128
+//                  (tcgen05.mma.cta_group::1);
+//   kPair = true   a cluster of two CTAs on two SMs shares a 256 x BN tile
+//                  (tcgen05.mma.cta_group::2, M=256): each CTA loads its 128
+//                  rows of A and half of the BN columns of B, holds 128 rows of
+//                  D in its TMEM, and the leader CTA (rank 0) issues the MMAs.
+//                  Per SM this halves the B tile in shared memory, so stages
+//                  are smaller (more of them fit) and the tensor core reads
+//                  less shared memory per flop.
 //
 // Two hardware facts shape the fp32-accurate mode (both pinned by GPU tests):
 //  * a TF32 MMA reads an fp32 operand truncated to its top 19 bits, so the raw
@@ -14,14 +25,15 @@
 //    *partial*, which the epilogue warps add into a TMEM *master* with fp32
 //    round-to-nearest adds; the error then no longer grows with K.
 //
-// Roles (448 threads = 14 warps, one CTA per SM):
+// Roles (448 threads = 14 warps per CTA, one CTA per SM):
 //   warps 0-7   epilogue: warp w owns TMEM lanes 32(w%4).. (tile rows) and the
 //               column half w/4. Per chunk: master (+)= partial. Per tile:
 //               alpha / bias / beta / store from the master; the row softmax
 //               runs in warps 0-3 with one thread per full row.
-//   warps 8-11  split (3xTF32 only): lo tile of every landed stage.
-//   warp 12     TMA producer (one lane).
-//   warp 13     TMEM allocator; one lane issues tcgen05.mma.
+//   warps 8-11  split (3xTF32): lo tile of every landed stage; in both modes
+//               they report the landed stage to the MMA issuer.
+//   warp 12     TMA producer (one lane), into this CTA's shared memory.
+//   warp 13     TMEM allocator; one lane (of the leader CTA) issues tcgen05.mma.
 // TMEM: columns [0, BN) partial, [BN, 2BN) master.
 //
 // Operand layouts in shared memory (per stage, 1024-byte aligned):
@@ -33,7 +45,9 @@
 //     4 KB spacing, 128-byte rows swizzled in 32-byte chunks; descriptor
 //     LBO 4096 B (next 32 MN), SBO 512 B (next 4 K rows); +1024 B per 8-deep
 //     K step.
-// Transposed views are therefore read in place; nothing is materialised.
+// Transposed views are therefore read in place; nothing is materialised. All
+// TMA loads are plain loads from this GPU's memory into the loading CTA's own
+// shared memory (no multicast).
 //
 // Every wait is bounded (global timer). On expiry the kernel records
 // MG_ERR_TIMEOUT in the device status word, every role stops, in-flight TMA
@@ -46,13 +60,14 @@
 
 namespace mg {
 
-constexpr int kBM = 128;            // tile rows (MMA M)
+constexpr int kBM = 128;            // tile rows per CTA (MMA M per SM)
 constexpr int kBK = 32;             // K elements per stage (128 bytes of fp32)
 constexpr int kChunkKb = 8;         // K-blocks accumulated in TMEM before promotion
 constexpr int kMaxStages = 8;
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
 constexpr int kSplitWarp0 = 8;
+constexpr int kSplitThreads = 128;
 constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
 constexpr int kThreads = 14 * 32;
@@ -77,7 +92,7 @@ enum : int {
 struct GemmParams {
     int M, N, K;
     int num_kb;                 // ceil(K / 32)
-    int m_tiles, n_tiles;
+    int m_tiles, n_tiles;       // tiles of (128 or 256 for pairs) x BN
     int tiles_per_batch;
     int total_tiles;
     int group_m;                // tile raster: group_m m-tiles sweep all n-tiles
@@ -135,12 +150,13 @@ __device__ __forceinline__ void batch_index(int b, const GemmParams& p, int* idx
 }
 
 struct SharedState {
-    uint64_t full[kMaxStages];
-    uint64_t split_done[kMaxStages];
-    uint64_t empty[kMaxStages];
-    uint64_t part_full;
-    uint64_t part_free;
-    uint64_t master_free;       // softmax mode: warps 0-3 finished reading a tile's master
+    uint64_t full[kMaxStages];        // local: TMA landed
+    uint64_t split_done[kMaxStages];  // MMA issuer's CTA: stage ready in every CTA
+    uint64_t empty[kMaxStages];       // local: the MMAs reading the stage are done
+    uint64_t part_full;               // local: partial accumulator complete
+    uint64_t part_free;               // MMA issuer's CTA: every epilogue took the partial
+    uint64_t master_done;             // local (softmax): every epilogue thread wrote its master half
+    uint64_t master_free;             // local (softmax): warps 0-3 finished reading the master
     uint64_t drain;
     uint32_t tmem_base;
     volatile int abort_flag;
@@ -156,19 +172,26 @@ __device__ __forceinline__ void record_failure(const GemmParams& p, SharedState*
 
 // Bounded wait for the phase of parity `parity` of `bar`. Returns false when
 // the CTA is aborting (another role gave up) or this wait itself ran out.
-template <bool kSleep>
+// kHow: 0 = poll (latency-critical single threads), 1 = poll with a suspend
+// hint (groups of waiting warps), 2 = poll with cluster-scope acquire (the
+// arrivals come from both CTAs of a pair).
+template <int kHow>
 __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, SharedState* ss,
                                            const GemmParams& p, int where)
 {
-    if (mbar_test(bar, parity)) return true;
+    auto test = [&]() {
+        if (kHow == 2) return mbar_test_cluster(bar, parity);
+        return mbar_test(bar, parity);
+    };
+    if (test()) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
-        if (kSleep) {
+        if (kHow == 1) {
             if (mbar_test_sleep(bar, parity, kSleepHintNs)) return true;
         } else {
 #pragma unroll 1
             for (int i = 0; i < 16; ++i)
-                if (mbar_test(bar, parity)) return true;
+                if (test()) return true;
         }
         if (ss->abort_flag) return false;
         if (global_timer_ns() - t0 > kWaitLimitNs) {
@@ -187,12 +210,14 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity)
     }
 }
 
-template <int BN>
+template <int BN, bool kPair>
 struct Layout {
+    static constexpr int kBRows = kPair ? BN / 2 : BN;       // B rows (N) this CTA loads
     static constexpr uint32_t kABytes = kBM * 128;          // 16 KB
-    static constexpr uint32_t kBBytes = BN * 128;
+    static constexpr uint32_t kBBytes = kBRows * 128;
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kTmemCols = 2 * BN;           // partial + master
+    static constexpr int kTileRows = kPair ? 2 * kBM : kBM;  // output rows per tile
 };
 
 __device__ __forceinline__ void store_row_chunk(float* crow, int gn0, int nvalid, const float* v)
@@ -208,13 +233,13 @@ __device__ __forceinline__ void store_row_chunk(float* crow, int gn0, int nvalid
     }
 }
 
-template <int BN>
+template <int BN, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     mg_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ GemmParams p)
 {
-    using L = Layout<BN>;
+    using L = Layout<BN, kPair>;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -231,15 +256,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const bool issuer = rank == 0;
+    // work unit: a tile per CTA, or a tile per pair (both CTAs walk the same list)
+    const int unit0 = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+    const int unit_step = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(&ss->full[s]), 1);
-            mbar_init(smem_u32(&ss->split_done[s]), 128);
+            mbar_init(smem_u32(&ss->split_done[s]), kSplitThreads * (kPair ? 2 : 1));
             mbar_init(smem_u32(&ss->empty[s]), 1);
         }
         mbar_init(smem_u32(&ss->part_full), 1);
-        mbar_init(smem_u32(&ss->part_free), kEpiThreads);
+        mbar_init(smem_u32(&ss->part_free), kEpiThreads * (kPair ? 2 : 1));
+        mbar_init(smem_u32(&ss->master_done), kEpiThreads);
         mbar_init(smem_u32(&ss->master_free), kEpiThreads / 2);
         mbar_init(smem_u32(&ss->drain), 1);
         ss->abort_flag = 0;
@@ -250,13 +281,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_map(&tmB);
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(smem_u32(&ss->tmem_base), L::kTmemCols);
-        tmem_relinquish();
+        if (kPair) {
+            tmem_alloc_pair(smem_u32(&ss->tmem_base), L::kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(&ss->tmem_base), L::kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (kPair) cluster_sync_all();   // the peer's barriers exist before any remote arrive
     tc_fence_after();
     const uint32_t tmem_base = ss->tmem_base;
+    // barriers of the MMA issuer's CTA, as shared::cluster addresses
+    const uint32_t split_done0 = kPair ? cluster_map(smem_u32(&ss->split_done[0]), 0) : smem_u32(&ss->split_done[0]);
+    const uint32_t part_free0 = kPair ? cluster_map(smem_u32(&ss->part_free), 0) : smem_u32(&ss->part_free);
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------ TMA producer
@@ -265,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_par = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+            for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
                 const TileCoord tc = decode_tile(t, p);
                 int idx[kMaxBatchDims];
                 batch_index(tc.batch, p, idx);
@@ -283,10 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         b4 += p.b_map[d] == 2 ? vb : 0;
                     }
                 }
-                const int m0 = tc.mt * kBM;
-                const int n0 = tc.nt * BN;
+                const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
+                const int n0 = tc.nt * BN + (int)rank * L::kBRows;
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!wait_phase<false>(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
+                    if (!wait_phase<0>(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
                         ok = false;
                         break;
                     }
@@ -304,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load(&tmB, fb, b_raw(stage), p.b_rank, k0, n0, b2, b3, b4);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < BN / 32; ++j)
+                        for (int j = 0; j < L::kBRows / 32; ++j)
                             tma_load(&tmB, fb, b_raw(stage) + 4096u * j, p.b_rank, n0 + 32 * j, k0, b2, b3, b4);
                     }
                     issued |= 1u << stage;
@@ -320,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == kMmaWarp) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        // ------------------------------------------------ MMA issuer (leader CTA)
+        if (lane == 0 && issuer) {
             const bool split = p.split != 0;
             const uint32_t a_lbo = p.a_mn ? 4096u : 16u;
             const uint32_t b_lbo = p.b_mn ? 4096u : 16u;
@@ -332,25 +372,32 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
             const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
             const uint32_t d_tmem = tmem_base;   // partial accumulator, columns [0, BN)
+            auto mma = [&](uint64_t da, uint64_t db, uint32_t acc) {
+                if (kPair) tc_mma_tf32_pair(d_tmem, da, db, p.idesc, acc);
+                else tc_mma_tf32(d_tmem, da, db, p.idesc, acc);
+            };
+            auto commit_all = [&](uint32_t bar) {   // arrive in every CTA of the pair
+                if (kPair) tc_commit_pair_all(bar, (uint16_t)0x3);
+                else tc_commit(bar);
+            };
             int stage = 0;
             uint32_t phase = 0;
             uint32_t chunk_phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+            for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     const bool chunk_start = (kb % kChunkKb) == 0;
                     const bool chunk_end = (kb % kChunkKb) == kChunkKb - 1 || kb == p.num_kb - 1;
                     if (chunk_start) {
-                        // the epilogue has taken the previous partial
-                        if (!wait_phase<false>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
-                                               kWaitMmaPartialFree)) {
+                        // every epilogue has taken the previous partial
+                        if (!wait_phase<kPair ? 2 : 0>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
+                                                       kWaitMmaPartialFree)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                     }
-                    const uint32_t ready = split ? smem_u32(&ss->split_done[stage]) : smem_u32(&ss->full[stage]);
-                    if (!wait_phase<false>(ready, phase, ss, p, kWaitMmaStage)) {
+                    if (!wait_phase<kPair ? 2 : 0>(smem_u32(&ss->split_done[stage]), phase, ss, p, kWaitMmaStage)) {
                         ok = false;
                         break;
                     }
@@ -363,39 +410,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                         if (split) {
                             const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                            tc_mma_tf32(d_tmem, dal, db, p.idesc, accum);   // lo * hi
-                            tc_mma_tf32(d_tmem, da, dbl, p.idesc, 1u);      // hi * lo
-                            tc_mma_tf32(d_tmem, da, db, p.idesc, 1u);       // hi * hi
+                            mma(dal, db, accum);   // lo * hi
+                            mma(da, dbl, 1u);      // hi * lo
+                            mma(da, db, 1u);       // hi * hi
                         } else {
-                            tc_mma_tf32(d_tmem, da, db, p.idesc, accum);
+                            mma(da, db, accum);
                         }
                     }
-                    tc_commit(smem_u32(&ss->empty[stage]));   // frees the stage when these MMAs finish
+                    commit_all(smem_u32(&ss->empty[stage]));   // frees the stage in every CTA
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
                     if (chunk_end) {
-                        tc_commit(smem_u32(&ss->part_full)); // partial ready for promotion
+                        commit_all(smem_u32(&ss->part_full));  // partial ready for promotion
                         chunk_phase ^= 1u;
                     }
                 }
             }
             // every MMA this thread issued has finished before TMEM is freed
-            tc_commit(smem_u32(&ss->drain));
+            if (kPair) tc_commit_pair(smem_u32(&ss->drain));
+            else tc_commit(smem_u32(&ss->drain));
             drain_phase(smem_u32(&ss->drain), 0);
         }
         __syncwarp();
     } else if (warp >= kSplitWarp0) {
-        // ------------------------------------------------ 3xTF32 split
-        if (p.split) {
-            const int tid = threadIdx.x - kSplitWarp0 * 32;
-            int stage = 0;
-            uint32_t phase = 0;
-            bool ok = true;
-            for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
-                for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!wait_phase<true>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)) {
-                        ok = false;
-                        break;
-                    }
+        // ------------------------------------------------ split / stage relay
+        const int tid = threadIdx.x - kSplitWarp0 * 32;
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!wait_phase<1>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)) {
+                    ok = false;
+                    break;
+                }
+                if (p.split) {
                     // The MMA reads the raw tile as hi (the TF32 datapath drops the
                     // 13 low mantissa bits); lo = x - hi is exact. Non-finite x
                     // gets lo = 0 so it passes through hi alone.
@@ -403,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint4* lo = reinterpret_cast<uint4*>(smem + (size_t)stage * L::kStageBytes + raw_region);
                     constexpr int n4 = (int)(L::kStageBytes / 16);
 #pragma unroll 4
-                    for (int i = tid; i < n4; i += 128) {
+                    for (int i = tid; i < n4; i += kSplitThreads) {
                         const uint4 x = raw[i];
                         uint4 l;
                         l.x = ((x.x & 0x7F800000u) == 0x7F800000u) ? 0u
@@ -417,9 +465,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         lo[i] = l;
                     }
                     fence_proxy_async_smem();
-                    mbar_arrive(smem_u32(&ss->split_done[stage]));
-                    if (++stage == stages) { stage = 0; phase ^= 1u; }
                 }
+                // stage ready (in this CTA) for the MMA issuer
+                if (kPair) mbar_arrive_cluster(split_done0 + (uint32_t)stage * 8u);
+                else mbar_arrive(smem_u32(&ss->split_done[stage]));
+                if (++stage == stages) { stage = 0; phase ^= 1u; }
             }
         }
     } else {
@@ -434,22 +484,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool has_bias = (p.epi & kEpiBias) != 0;
         const bool softmax = (p.epi & kEpiSoftmax) != 0;
         uint32_t chunk_phase = 0;
+        uint32_t md_phase = 0;
         uint32_t mf_phase = 0;
         bool ok = true;
-        for (int t = blockIdx.x; ok && t < p.total_tiles; t += gridDim.x) {
+        for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
             const TileCoord tc = decode_tile(t, p);
             const int n_chunks = (p.num_kb + kChunkKb - 1) / kChunkKb;
             if (softmax && half == 1) {
                 // warps 0-3 read the whole master row of the previous tile; do
                 // not overwrite this half before they are done with it
-                const bool freed = wait_phase<true>(smem_u32(&ss->master_free), mf_phase ^ 1u, ss, p,
-                                                    kWaitEpilogueMasterFree);
+                const bool freed = wait_phase<1>(smem_u32(&ss->master_free), mf_phase ^ 1u, ss, p,
+                                                 kWaitEpilogueMasterFree);
                 if (!__all_sync(0xffffffffu, freed)) break;
                 mf_phase ^= 1u;
             }
             // ---- promotions: master = sum of the tile's partials (fp32 round-to-nearest)
             for (int c = 0; c < n_chunks; ++c) {
-                const bool got = wait_phase<true>(smem_u32(&ss->part_full), chunk_phase, ss, p, kWaitEpiloguePartial);
+                const bool got = wait_phase<1>(smem_u32(&ss->part_full), chunk_phase, ss, p, kWaitEpiloguePartial);
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll 1
@@ -466,14 +517,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(t_master + j, r);
                 }
                 tc_fence_before();
-                mbar_arrive(smem_u32(&ss->part_free));   // the MMA may overwrite the partial
+                // the MMA may overwrite the partial once every epilogue has it
+                if (kPair) mbar_arrive_cluster(part_free0);
+                else mbar_arrive(smem_u32(&ss->part_free));
                 chunk_phase ^= 1u;
             }
             if (!ok) break;
             if (softmax) {
-                // all 256 epilogue threads have written their master columns
-                const bool synced = wait_phase<true>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
-                                                     kWaitEpilogueMaster);
+                // every epilogue thread of this CTA has written its master columns
+                mbar_arrive(smem_u32(&ss->master_done));
+                const bool synced = wait_phase<1>(smem_u32(&ss->master_done), md_phase, ss, p, kWaitEpilogueMaster);
+                md_phase ^= 1u;
                 if (!__all_sync(0xffffffffu, synced)) break;
                 tc_fence_after();
             }
@@ -489,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     boff += (int64_t)idx[d] * p.bias_bs[d];
                 }
             }
-            const int m0 = tc.mt * kBM;
+            const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
             const int n0 = tc.nt * BN;
             const int gm = m0 + row;
             const bool rok = gm < p.M;
@@ -497,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float* brow = has_bias ? p.bias + boff + (int64_t)(rok ? gm : 0) * p.bias_rs : nullptr;
             const uint32_t t_row = lane_base + (uint32_t)BN;   // master, column 0
 
-            if (p.epi & kEpiSoftmax) {
+            if (softmax) {
                 // Warps 0-3: one thread owns one full row (N <= BN, single
                 // n-tile), so the row softmax needs no cross-thread reduction.
                 if (half == 0) {
@@ -580,9 +634,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if (kPair) cluster_sync_all();   // the leader's MMAs no longer touch the peer
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, L::kTmemCols);
+        if (kPair) tmem_dealloc_pair(tmem_base, L::kTmemCols);
+        else tmem_dealloc(tmem_base, L::kTmemCols);
     }
 }
 

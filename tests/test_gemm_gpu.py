@@ -171,6 +171,52 @@ def test_batched_broadcast_layouts(sa, sb, ta, tb, mode):
     assert_close(gpu_matmul(A, B, ta, tb), ob.oracle_matmul(A, B, ta, tb), mode, f"{sa}x{sb}")
 
 
+@pytest.fixture(params=["0", "1"], ids=["single_sm", "sm_pair"])
+def kernel_variant(request, monkeypatch):
+    """Forces the single-SM (M=128 tiles) or the SM-pair (M=256 tiles,
+    cta_group::2) kernel through MG_GEMM_PAIR, which the library reads on
+    every call."""
+    monkeypatch.setenv("MG_GEMM_PAIR", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("sa,sb,ta,tb,bias_shape", [
+    ((300, 520), (520, 200), False, False, None),          # M, N tails in both tiles
+    ((2, 260, 96), (2, 300, 96), False, True, (300,)),     # K-major B, bias
+    ((3, 64, 400), (64, 130), True, False, None),          # MN-major A and B
+    ((520, 70), (40, 520), True, True, (70, 1)),           # both transposed, column bias
+    ((4, 256, 64), (4, 256, 64), False, True, None),       # attention-score shape
+])
+def test_kernel_variants_agree_with_oracle(kernel_variant, mode, sa, sb, ta, tb, bias_shape):
+    set_mode(mode)
+    A = ob.seeded_uniform(sa, 801)
+    B = ob.seeded_uniform(sb, 802)
+    bias = ob.seeded_uniform(bias_shape, 803) if bias_shape else None
+    assert_close(gpu_matmul(A, B, ta, tb, bias), ob.oracle_matmul(A, B, ta, tb, bias), mode,
+                 f"variant {kernel_variant}")
+
+
+def test_kernel_variants_softmax_and_accumulate(kernel_variant):
+    set_mode(_lib.MG_MODE_TF32X3)
+    q = ob.seeded_normal((3, 2, 200, 64), 811, 0.0, 0.125)
+    k = ob.seeded_normal((3, 2, 200, 64), 812, 0.0, 0.125)
+    P = host(F.attention_scores(cuda(q), cuda(k), 0.125, causal=True))
+    mask = ob.oracle_causal_mask(200)
+    for b in range(3):
+        for h in range(2):
+            S = ob.oracle_matmul(q[b, h] * np.float32(0.125), k[b, h], False, True, mask)
+            assert_close(P[b, h], ob.oracle_softmax_rows(S), 0, f"softmax {kernel_variant}")
+    A = ob.seeded_uniform((4, 300, 48), 813)
+    W = ob.seeded_uniform((48, 80), 814)
+    dC = ob.seeded_normal((4, 300, 80), 815)
+    prev = ob.seeded_normal((48, 80), 816)
+    g = cuda(prev)
+    F.matmul_backward(cuda(A), cuda(W), cuda(dC), need_a=False, grad_b=g)
+    _, dW, _ = ob.oracle_matmul_backward(A, W, dC)
+    assert_close(host(g), prev + dW, 0, f"beta=1 {kernel_variant}")
+
+
 @pytest.mark.parametrize("bias_shape", [(40,), (1, 40), (30, 1), (30, 40), (3, 1, 40), (3, 30, 40)])
 def test_bias_broadcast_forms(bias_shape):
     set_mode(_lib.MG_MODE_TF32X3)
