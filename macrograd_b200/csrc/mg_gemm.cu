@@ -242,6 +242,29 @@ __global__ void pad_copy_kernel(PadParams p)
     for (int64_t c = threadIdx.x; c < p.dst_ld; c += blockDim.x) o[c] = c < p.cols ? s[c] : 0.f;
 }
 
+// lo plane of the 3xTF32 split over an operand's storage span: lo = x - hi,
+// hi = x with its 13 low mantissa bits cleared (0 for non-finite x). One HBM
+// pass (4 bytes read, 4 written per element); the GEMM then loads hi (the raw
+// operand) and lo tiles instead of splitting every tile it loads.
+__global__ void lo_plane_kernel(const float* __restrict__ x, float* __restrict__ lo, int64_t n)
+{
+    const int64_t n4 = n / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* l4 = reinterpret_cast<float4*>(lo);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const float4 v = x4[i];
+        float4 r;
+        r.x = __uint_as_float(mg::split_lo(__float_as_uint(v.x)));
+        r.y = __uint_as_float(mg::split_lo(__float_as_uint(v.y)));
+        r.z = __uint_as_float(mg::split_lo(__float_as_uint(v.z)));
+        r.w = __uint_as_float(mg::split_lo(__float_as_uint(v.w)));
+        l4[i] = r;
+    }
+    for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        lo[i] = __uint_as_float(mg::split_lo(__float_as_uint(x[i])));
+}
+
 // K == 0: C = bias (+ beta C), or the softmax of the bias / mask alone.
 struct FillParams {
     int M, N, nbd;
@@ -293,7 +316,7 @@ __global__ void k0_fill_kernel(FillParams p)
 // pieces of that fixed buffer instead and never allocates or frees.
 struct Workspace {
     void* stream;
-    void* ptrs[2] = {nullptr, nullptr};
+    void* ptrs[4] = {nullptr, nullptr, nullptr, nullptr};
     int n = 0;
     uint8_t* arena = nullptr;
     size_t arena_cap = 0, arena_used = 0;
@@ -377,8 +400,8 @@ mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace&
 }
 
 template <int BN, bool kPair>
-mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb,
-                    mg::GemmParams& gp, cudaStream_t st)
+mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& malo,
+                    const CUtensorMap& mblo, mg::GemmParams& gp, cudaStream_t st)
 {
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
@@ -417,14 +440,46 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         }
         const int pairs = std::max(1, std::min(gp.total_tiles, dev->max_clusters[slot - 3]));
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, gp));
+        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp));
     } else {
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
-        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, gp);
+        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, gp);
         MG_CUDA_TRY(cudaGetLastError());
     }
     g_launches++;
     return MG_OK;
+}
+
+// Tuning override from the environment (clamped), else the default.
+int tuning_int(const char* name, int dflt, int lo, int hi)
+{
+    if (const char* e = std::getenv(name)) {
+        const int v = std::atoi(e);
+        if (v >= lo && v <= hi) return v;
+    }
+    return dflt;
+}
+
+// Elements from an operand's first to its last element, as its tensor map
+// addresses them: the storage a same-layout lo plane needs.
+int64_t operand_span(const Operand& x, const BatchMap& bm)
+{
+    int64_t span = (x.rows - 1) * x.ld + x.cols;
+    for (int j = 0; j < bm.nmap; ++j) span += (bm.extent[j] - 1) * bm.stride[j];
+    return span;
+}
+
+// Pre-split pays one HBM pass over both operands and workspace of their size,
+// and doubles the bytes each stage loads; in-kernel splitting repeats the
+// split once per tile that loads an operand tile. Measured at 8192^3 the
+// in-kernel split is faster (189 vs 184 TFLOP/s, median of 3), so pre-split
+// is off unless MG_GEMM_PRESPLIT=1 asks for it.
+bool want_presplit(double flops, int64_t m_tiles, int64_t n_tiles)
+{
+    if (const char* e = std::getenv("MG_GEMM_PRESPLIT")) {
+        if (e[0] == '1') return flops > 0 && m_tiles > 0 && n_tiles > 0;
+    }
+    return false;
 }
 
 // Pair kernel (two SMs per 256-row tile) when a batch has more than 128 rows;
@@ -590,6 +645,30 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     s = encode_map(&mb, b, bmp, b_mn, (uint32_t)b_rows);
     if (s != MG_OK) return s;
 
+    // 3xTF32 on large problems: precompute the lo planes once (HBM pass) so the
+    // main loop loads hi and lo tiles instead of splitting every tile it loads.
+    const int64_t m_tiles_est = (d->M + tile_rows - 1) / tile_rows;
+    const int64_t n_tiles_est = (d->N + bn - 1) / bn;
+    const bool presplit = mode == MG_MODE_TF32X3 && arena == nullptr &&
+                          want_presplit(2.0 * d->M * d->N * d->K * (double)nbatch, m_tiles_est, n_tiles_est);
+    CUtensorMap malo = ma, mblo = mb;
+    if (presplit) {
+        for (int which = 0; which < 2; ++which) {
+            Operand x = which ? b : a;
+            const BatchMap& bm = which ? bmp : am;
+            const int64_t span = operand_span(x, bm);
+            float* lo = static_cast<float*>(ws.get((size_t)span * sizeof(float) + 16));
+            if (!lo) return fail(MG_ERR_ALLOC, "workspace allocation of %lld bytes failed", (long long)(span * 4));
+            const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>((span / 4 + 255) / 256, 8ll * dev->sm_count));
+            lo_plane_kernel<<<(unsigned)blocks, 256, 0, st>>>(x.ptr, lo, span);
+            MG_CUDA_TRY(cudaGetLastError());
+            g_launches++;
+            x.ptr = lo;
+            s = which ? encode_map(&mblo, x, bm, b_mn, (uint32_t)b_rows) : encode_map(&malo, x, bm, a_mn, mg::kBM);
+            if (s != MG_OK) return s;
+        }
+    }
+
     mg::GemmParams gp;
     std::memset(&gp, 0, sizeof(gp));
     gp.M = d->M;
@@ -603,7 +682,10 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     if (total >= (1ll << 31)) return fail(MG_ERR_UNSUPPORTED, "too many output tiles (%lld)", (long long)total);
     gp.total_tiles = (int)total;
     gp.group_m = 16;
+    gp.chunk_kb = tuning_int("MG_GEMM_CHUNK_KB", mg::kChunkKb, 1, 64);
+    gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);
     gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
+    gp.presplit = presplit ? 1 : 0;
     gp.a_mn = a_mn;
     gp.b_mn = b_mn;
     gp.a_rank = 2 + am.nmap;
@@ -633,15 +715,15 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
 
     if (pair) {
         switch (bn) {
-        case 64: return launch_tc<64, true>(dev, ma, mb, gp, st);
-        case 128: return launch_tc<128, true>(dev, ma, mb, gp, st);
-        default: return launch_tc<256, true>(dev, ma, mb, gp, st);
+        case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, st);
+        case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, st);
+        default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, st);
         }
     }
     switch (bn) {
-    case 64: return launch_tc<64, false>(dev, ma, mb, gp, st);
-    case 128: return launch_tc<128, false>(dev, ma, mb, gp, st);
-    default: return launch_tc<256, false>(dev, ma, mb, gp, st);
+    case 64: return launch_tc<64, false>(dev, ma, mb, malo, mblo, gp, st);
+    case 128: return launch_tc<128, false>(dev, ma, mb, malo, mblo, gp, st);
+    default: return launch_tc<256, false>(dev, ma, mb, malo, mblo, gp, st);
     }
 }
 

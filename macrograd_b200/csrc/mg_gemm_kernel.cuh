@@ -62,7 +62,7 @@ namespace mg {
 
 constexpr int kBM = 128;            // tile rows per CTA (MMA M per SM)
 constexpr int kBK = 32;             // K elements per stage (128 bytes of fp32)
-constexpr int kChunkKb = 8;         // K-blocks accumulated in TMEM before promotion
+constexpr int kChunkKb = 8;         // default K-blocks accumulated in TMEM before promotion
 constexpr int kMaxStages = 8;
 constexpr int kEpiWarps = 8;
 constexpr int kEpiThreads = kEpiWarps * 32;
@@ -97,7 +97,10 @@ struct GemmParams {
     int total_tiles;
     int group_m;                // tile raster: group_m m-tiles sweep all n-tiles
     int stages;
+    int chunk_kb;               // K-blocks per TMEM partial (promotion interval)
+    int relay_spin;             // split warps poll without suspend hints
     int split;                  // 1 = 3xTF32
+    int presplit;               // 3xTF32 with lo planes precomputed in HBM (tmAlo / tmBlo)
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
     int a_rank, b_rank;         // tensor-map ranks (2 + mapped batch dims)
     uint32_t idesc;
@@ -220,6 +223,14 @@ struct Layout {
     static constexpr int kTileRows = kPair ? 2 * kBM : kBM;  // output rows per tile
 };
 
+// lo = x - hi of the 3xTF32 split, hi = x with its 13 low mantissa bits
+// cleared; exact in fp32. Non-finite x gives lo = 0, so it passes through hi.
+__device__ __forceinline__ uint32_t split_lo(uint32_t x)
+{
+    const float d = __uint_as_float(x) - __uint_as_float(x & 0xFFFFE000u);
+    return d == d ? __float_as_uint(d) : 0u;
+}
+
 __device__ __forceinline__ void store_row_chunk(float* crow, int gn0, int nvalid, const float* v)
 {
     if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(crow + gn0) & 15u) == 0)) {
@@ -233,10 +244,15 @@ __device__ __forceinline__ void store_row_chunk(float* crow, int gn0, int nvalid
     }
 }
 
+// tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
+// tmBlo map their lo planes (same layout), which the producer loads next to
+// the raw tiles instead of the split warps computing them.
 template <int BN, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     mg_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmAlo,
+                      const __grid_constant__ CUtensorMap tmBlo,
                       const __grid_constant__ GemmParams p)
 {
     using L = Layout<BN, kPair>;
@@ -279,6 +295,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp && lane == 0) {
         tma_prefetch_map(&tmA);
         tma_prefetch_map(&tmB);
+        if (p.presplit) {
+            tma_prefetch_map(&tmAlo);
+            tma_prefetch_map(&tmBlo);
+        }
     }
     if (warp == kMmaWarp) {
         if (kPair) {
@@ -331,21 +351,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&ss->full[stage]);
-                    mbar_arrive_expect_tx(fb, L::kStageBytes);
+                    mbar_arrive_expect_tx(fb, L::kStageBytes * (p.presplit ? 2u : 1u));
                     const int k0 = kb * kBK;
-                    if (!p.a_mn) {
-                        tma_load(&tmA, fb, a_raw(stage), p.a_rank, k0, m0, a2, a3, a4);
-                    } else {
+                    // raw tiles, and in pre-split mode the lo tiles one region higher
+                    for (int plane = 0; plane < (p.presplit ? 2 : 1); ++plane) {
+                        const CUtensorMap* ma = plane ? &tmAlo : &tmA;
+                        const CUtensorMap* mb = plane ? &tmBlo : &tmB;
+                        const uint32_t da = plane ? a_lo(stage) : a_raw(stage);
+                        const uint32_t db = plane ? b_lo(stage) : b_raw(stage);
+                        if (!p.a_mn) {
+                            tma_load(ma, fb, da, p.a_rank, k0, m0, a2, a3, a4);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < kBM / 32; ++j)
-                            tma_load(&tmA, fb, a_raw(stage) + 4096u * j, p.a_rank, m0 + 32 * j, k0, a2, a3, a4);
-                    }
-                    if (!p.b_mn) {
-                        tma_load(&tmB, fb, b_raw(stage), p.b_rank, k0, n0, b2, b3, b4);
-                    } else {
+                            for (int j = 0; j < kBM / 32; ++j)
+                                tma_load(ma, fb, da + 4096u * j, p.a_rank, m0 + 32 * j, k0, a2, a3, a4);
+                        }
+                        if (!p.b_mn) {
+                            tma_load(mb, fb, db, p.b_rank, k0, n0, b2, b3, b4);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < L::kBRows / 32; ++j)
-                            tma_load(&tmB, fb, b_raw(stage) + 4096u * j, p.b_rank, n0 + 32 * j, k0, b2, b3, b4);
+                            for (int j = 0; j < L::kBRows / 32; ++j)
+                                tma_load(mb, fb, db + 4096u * j, p.b_rank, n0 + 32 * j, k0, b2, b3, b4);
+                        }
                     }
                     issued |= 1u << stage;
                     issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
@@ -386,8 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    const bool chunk_start = (kb % kChunkKb) == 0;
-                    const bool chunk_end = (kb % kChunkKb) == kChunkKb - 1 || kb == p.num_kb - 1;
+                    const bool chunk_start = (kb % p.chunk_kb) == 0;
+                    const bool chunk_end = (kb % p.chunk_kb) == p.chunk_kb - 1 || kb == p.num_kb - 1;
                     if (chunk_start) {
                         // every epilogue has taken the previous partial
                         if (!wait_phase<kPair ? 2 : 0>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
@@ -433,36 +460,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp >= kSplitWarp0) {
         // ------------------------------------------------ split / stage relay
+        // Every thread waits for the stage itself and reports it itself: a
+        // warp-wide wait / arrive is one warp instruction, and no thread is held
+        // back by another's wake-up.
         const int tid = threadIdx.x - kSplitWarp0 * 32;
+        const bool compute_lo = p.split && !p.presplit;
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
         for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                if (!wait_phase<1>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)) {
+                const bool landed = p.relay_spin
+                    ? wait_phase<0>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)
+                    : wait_phase<1>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull);
+                if (!landed) {
                     ok = false;
                     break;
                 }
-                if (p.split) {
+                if (compute_lo) {
                     // The MMA reads the raw tile as hi (the TF32 datapath drops the
-                    // 13 low mantissa bits); lo = x - hi is exact. Non-finite x
-                    // gets lo = 0 so it passes through hi alone.
+                    // 13 low mantissa bits); lo = x - hi is exact.
                     const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes);
                     uint4* lo = reinterpret_cast<uint4*>(smem + (size_t)stage * L::kStageBytes + raw_region);
                     constexpr int n4 = (int)(L::kStageBytes / 16);
 #pragma unroll 4
                     for (int i = tid; i < n4; i += kSplitThreads) {
                         const uint4 x = raw[i];
-                        uint4 l;
-                        l.x = ((x.x & 0x7F800000u) == 0x7F800000u) ? 0u
-                              : __float_as_uint(__uint_as_float(x.x) - __uint_as_float(x.x & 0xFFFFE000u));
-                        l.y = ((x.y & 0x7F800000u) == 0x7F800000u) ? 0u
-                              : __float_as_uint(__uint_as_float(x.y) - __uint_as_float(x.y & 0xFFFFE000u));
-                        l.z = ((x.z & 0x7F800000u) == 0x7F800000u) ? 0u
-                              : __float_as_uint(__uint_as_float(x.z) - __uint_as_float(x.z & 0xFFFFE000u));
-                        l.w = ((x.w & 0x7F800000u) == 0x7F800000u) ? 0u
-                              : __float_as_uint(__uint_as_float(x.w) - __uint_as_float(x.w & 0xFFFFE000u));
-                        lo[i] = l;
+                        lo[i] = make_uint4(split_lo(x.x), split_lo(x.y), split_lo(x.z), split_lo(x.w));
                     }
                     fence_proxy_async_smem();
                 }
@@ -489,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
             const TileCoord tc = decode_tile(t, p);
-            const int n_chunks = (p.num_kb + kChunkKb - 1) / kChunkKb;
+            const int n_chunks = (p.num_kb + p.chunk_kb - 1) / p.chunk_kb;
             if (softmax && half == 1) {
                 // warps 0-3 read the whole master row of the previous tile; do
                 // not overwrite this half before they are done with it
@@ -517,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32(t_master + j, r);
                 }
                 tc_fence_before();
-                // the MMA may overwrite the partial once every epilogue has it
+                // the MMA may overwrite the partial once every epilogue thread has it
                 if (kPair) mbar_arrive_cluster(part_free0);
                 else mbar_arrive(smem_u32(&ss->part_free));
                 chunk_phase ^= 1u;

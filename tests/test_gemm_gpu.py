@@ -197,6 +197,25 @@ def test_kernel_variants_agree_with_oracle(kernel_variant, mode, sa, sb, ta, tb,
                  f"variant {kernel_variant}")
 
 
+@pytest.mark.parametrize("presplit", ["0", "1"], ids=["split_in_kernel", "lo_planes"])
+@pytest.mark.parametrize("sa,sb,ta,tb,bias_shape", [
+    ((600, 520), (520, 700), False, False, None),
+    ((3, 520, 300), (1, 520, 260), True, False, (260,)),     # broadcast B, MN-major A
+    ((2, 2, 300, 96), (2, 1, 270, 96), False, True, None),  # 4-D, broadcast B over one dim
+    ((700, 33), (333, 700), True, True, None),               # odd K-major / MN-major widths
+])
+def test_presplit_paths_agree_with_oracle(kernel_variant, monkeypatch, presplit, sa, sb, ta, tb, bias_shape):
+    """3xTF32 with lo computed per tile in the kernel, and with lo planes
+    precomputed once in HBM (MG_GEMM_PRESPLIT forces either path)."""
+    monkeypatch.setenv("MG_GEMM_PRESPLIT", presplit)
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform(sa, 821)
+    B = ob.seeded_uniform(sb, 822)
+    bias = ob.seeded_uniform(bias_shape, 823) if bias_shape else None
+    assert_close(gpu_matmul(A, B, ta, tb, bias), ob.oracle_matmul(A, B, ta, tb, bias), 0,
+                 f"presplit={presplit} variant={kernel_variant}")
+
+
 def test_kernel_variants_softmax_and_accumulate(kernel_variant):
     set_mode(_lib.MG_MODE_TF32X3)
     q = ob.seeded_normal((3, 2, 200, 64), 811, 0.0, 0.125)
