@@ -2,7 +2,9 @@
 
 Workload: C = A @ B, A and B [8192, 8192] fp32 ~ U(-1, 1). The rows of A (and
 so of C) are split across the N ranks (one process per GPU), B is replicated,
-and when N > 1 the C rows are all-gathered over NCCL so every GPU holds C.
+and when N > 1 every GPU ends the step holding all of C: by default each rank's
+GEMM epilogue writes its rows into every GPU's C over NVLink (the all-gather
+fused into the kernel; --gather nccl uses an NCCL all-gather after the GEMM).
 Work is fixed as N grows ("strong" scaling). Default mode 3xTF32
 (fp32-accurate); --mode tf32 times the fast mode.
 
@@ -47,6 +49,9 @@ def parse_args():
     p.add_argument("--size", type=int, default=SIZE)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--gather", choices=["fused", "nccl"], default="fused",
+                   help="N>1: C rows reach every GPU from the GEMM epilogue over NVLink (fused) "
+                        "or by an NCCL all-gather after it")
     return p.parse_args()
 
 
@@ -210,7 +215,7 @@ def main():
     sys.path.insert(0, ROOT)
     import macrograd_b200 as mg
     from macrograd_b200 import _lib
-    from macrograd_b200.sharded import gather_rows, row_block, sharded_matmul
+    from macrograd_b200.sharded import PeerRows, gather_rows, row_block, scatter_matmul, sharded_matmul
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -231,9 +236,25 @@ def main():
     C_local = torch.empty(rows, n, device=dev)
     C_full = torch.empty(n, n, device=dev) if world > 1 else C_local
     stream = torch.cuda.current_stream(dev)
+    fused = world > 1 and args.gather == "fused"
+    peers = PeerRows(C_full) if fused else None
+    fence = torch.zeros(1, device=dev)
+
+    def gemm():
+        if fused:
+            scatter_matmul(A, B, peers, r0)               # rows into every GPU's C, from the epilogue
+        else:
+            sharded_matmul(A, B, local_out=C_local)       # this rank's rows (one GEMM launch)
+
+    def exchange():
+        if fused:
+            dist.all_reduce(fence)                        # every rank's rows have landed
+        elif world > 1:
+            gather_rows(C_full, C_local)                  # C rows to every GPU (NCCL)
 
     def step():
-        sharded_matmul(A, B, full_out=C_full if world > 1 else None, local_out=C_local)
+        gemm()
+        exchange()
 
     def barrier():
         if world > 1:
@@ -256,10 +277,9 @@ def main():
     ev0.record(stream)
     for i in range(args.steps):
         kern_ev[i][0].record(stream)
-        sharded_matmul(A, B, local_out=C_local)        # this rank's rows (one GEMM launch)
+        gemm()
         kern_ev[i][1].record(stream)
-        if world > 1:
-            gather_rows(C_full, C_local)                  # C rows to every GPU (NCCL)
+        exchange()
         kern_ev[i][2].record(stream)
     ev1.record(stream)
     torch.cuda.synchronize()
@@ -287,8 +307,13 @@ def main():
 
         def e2e_step():
             A_d.copy_(A_h, non_blocking=True)
-            sharded_matmul(A_d, B, full_out=C_full if world > 1 else None, local_out=C_local)
-            C_h.copy_(C_local, non_blocking=True)
+            if fused:
+                scatter_matmul(A_d, B, peers, r0)
+                dist.all_reduce(fence)
+                C_h.copy_(C_full[r0:r1], non_blocking=True)
+            else:
+                sharded_matmul(A_d, B, full_out=C_full if world > 1 else None, local_out=C_local)
+                C_h.copy_(C_local, non_blocking=True)
 
         for _ in range(2):
             e2e_step()
@@ -314,6 +339,9 @@ def main():
                        "own C rows device->host; B resident like weights"}
 
     if world > 1:
+        dist.barrier(device_ids=[local_rank])             # no rank still writes into a peer's C
+        if peers is not None:
+            peers.close()
         dist.destroy_process_group()
     if rank != 0:
         return 0
@@ -332,7 +360,9 @@ def main():
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic U(-1,1) (torch generator, seeded), resident in HBM",
         "config": {"workload": WORKLOAD, "size": n, "rows_per_gpu": rows,
-                   "mode": args.mode, "parallelism": f"row-shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "mode": args.mode,
+                   "parallelism": f"row-shard x{world}" + ((" + all-gather fused into the GEMM epilogue (NVLink peer stores)"
+                                                              if fused else " + NCCL all-gather") if world > 1 else ""),
                    "l2": "inputs larger than L2 (2 x 268 MB operands, 268 MB output)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak, "traffic": traffic,
@@ -343,8 +373,9 @@ def main():
         "e2e": e2e,
         "gpu_launches": int(launches),
         "gemm_only": {"value": flops / (kern_ms * 1e-3) / 1e12, "unit": UNIT, "ms": kern_ms,
-                      "note": "max over ranks of the per-rank GEMM time; the step adds the all-gather"},
-        "all_gather_ms": gather_ms if world > 1 else 0.0,
+                      "note": "max over ranks of the per-rank GEMM time; the step adds the exchange "
+                              "(the fence of the fused all-gather, or the NCCL all-gather)"},
+        "exchange_ms": gather_ms if world > 1 else 0.0,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

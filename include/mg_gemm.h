@@ -126,6 +126,31 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
                             int32_t rank, int32_t trans_a, int32_t trans_b,
                             float alpha, int32_t causal, void* stream);
 
+/* ---- multi-GPU: row-sharded GEMM with the all-gather fused into it ------
+ * No counterpart in the reference (single-GPU only, README.md:538). A job of
+ * R ranks (one process per GPU) splits the rows of A (and of C) into R blocks;
+ * B is replicated. Each rank runs mg_gemm_scatter_rows on its rows, and its
+ * epilogue writes every finished row chunk straight into the full C of every
+ * rank (peer_C[0..npeers), this rank's own included) at row row0 + m, over
+ * NVLink peer mappings -- so the all-gather travels while the tensor cores
+ * work, instead of after. No collective runs inside the kernel; the caller
+ * orders steps across ranks (e.g. a small NCCL all-reduce after the GEMM)
+ * before reading a C that other ranks write into, or overwriting it again.
+ * `d` describes this rank's GEMM (M = its rows); d->ldc is the row stride of
+ * the full C buffers; beta must be 0. */
+#define MG_MAX_PEERS 8
+mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const float* B,
+                               const float* bias, float* const* peer_C, int32_t npeers,
+                               int64_t row0, void* stream);
+
+/* CUDA IPC plumbing for peer_C: export a device buffer of this process
+ * (a handle plus the buffer's offset inside its allocation), and map a buffer
+ * another process exported (valid until mg_ipc_close). */
+typedef struct mg_ipc_handle { unsigned char bytes[64]; } mg_ipc_handle;
+mg_status mg_ipc_export(const void* dev_ptr, mg_ipc_handle* handle, uint64_t* offset);
+mg_status mg_ipc_import(const mg_ipc_handle* handle, uint64_t offset, void** dev_ptr);
+mg_status mg_ipc_close(void* dev_ptr);
+
 /* No counterpart in the reference: an allocation-free form of mg_matmul.
  *
  * Some callers cannot let a library allocate device memory during a call:

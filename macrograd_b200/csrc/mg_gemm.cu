@@ -54,6 +54,14 @@ DeviceState g_dev[kMaxDevices];
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+// Peer buffers mapped by mg_ipc_import: the pointer handed out and the base
+// cudaIpcOpenMemHandle returned (needed to unmap).
+struct IpcMap {
+    void* user = nullptr;
+    void* base = nullptr;
+};
+IpcMap g_ipc_maps[64];
+
 mg_status fail(mg_status s, const char* fmt, ...)
 {
     char buf[512];
@@ -405,7 +413,8 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
 {
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
-    const size_t fixed = 1024 + sizeof(mg::SharedState) + 64;
+    // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
+    const size_t fixed = 1024 + mg::kSharedStateBytes + (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4 + 64;
     const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);
     int stages = (int)((size_t)(dev->max_smem - (int)fixed) / per_stage);
     stages = std::min(stages, mg::kMaxStages);
@@ -550,8 +559,16 @@ void mg_gemm_desc_init(mg_gemm_desc* d, int32_t M, int32_t N, int32_t K, int32_t
 // The body of mg_gemm. With arena == nullptr the per-call scratch (operand
 // re-layout) is allocated as usual; with an arena it comes from that fixed
 // buffer and a request that does not fit is rejected before anything runs.
+// Destinations of a row-sharded GEMM whose rows go to every rank's full C.
+struct ScatterSpec {
+    int npeers;
+    int64_t row0;
+    float* peers[mg::kMaxPeers];
+};
+
 static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, const float* B,
-                           const float* bias, void* stream, uint8_t* arena, size_t arena_cap)
+                           const float* bias, void* stream, uint8_t* arena, size_t arena_cap,
+                           const ScatterSpec* scatter = nullptr)
 {
     g_last_error.clear();
     mg_status s = validate(d, C, A, B, bias);
@@ -712,6 +729,11 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.beta = d->beta;
     gp.epi = d->epilogue;
     gp.status = dev->status;
+    if (scatter) {
+        gp.npeers = scatter->npeers;
+        gp.peer_row0 = scatter->row0;
+        for (int q = 0; q < scatter->npeers; ++q) gp.peers[q] = scatter->peers[q];
+    }
 
     if (pair) {
         switch (bn) {
@@ -859,6 +881,90 @@ mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const in
         }
     }
     return gemm_impl(&d, out, A, B, nullptr, stream, g_noalloc_ptr[dev], MG_NOALLOC_SCRATCH_BYTES);
+}
+
+mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const float* B, const float* bias,
+                               float* const* peer_C, int32_t npeers, int64_t row0, void* stream)
+{
+    g_last_error.clear();
+    if (!d) return fail(MG_ERR_INVALID, "descriptor is NULL");
+    if (npeers < 1 || npeers > mg::kMaxPeers)
+        return fail(MG_ERR_INVALID, "npeers %d outside [1, %d]", npeers, mg::kMaxPeers);
+    if (!peer_C) return fail(MG_ERR_INVALID, "peer_C is NULL");
+    if (row0 < 0) return fail(MG_ERR_INVALID, "negative row offset");
+    if (d->beta != 0.f) return fail(MG_ERR_INVALID, "the scattering GEMM does not accumulate (beta must be 0)");
+    ScatterSpec sc;
+    sc.npeers = npeers;
+    sc.row0 = row0;
+    for (int q = 0; q < npeers; ++q) {
+        if (!peer_C[q]) return fail(MG_ERR_INVALID, "peer_C[%d] is NULL", q);
+        sc.peers[q] = peer_C[q];
+    }
+    if (d->K == 0) return fail(MG_ERR_UNSUPPORTED, "K = 0 is not supported by the scattering GEMM");
+    return gemm_impl(d, peer_C[0], A, B, bias, stream, nullptr, 0, &sc);
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(mg_ipc_handle), "IPC handle does not fit");
+
+mg_status mg_ipc_export(const void* dev_ptr, mg_ipc_handle* handle, uint64_t* offset)
+{
+    g_last_error.clear();
+    if (!dev_ptr || !handle || !offset) return fail(MG_ERR_INVALID, "NULL argument");
+    static PFN_cuMemGetAddressRange_v3020 get_range = nullptr;
+    if (!get_range) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        MG_CUDA_TRY(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
+        if (q != cudaDriverEntryPointSuccess || !fn) return fail(MG_ERR_CUDA, "cuMemGetAddressRange unavailable");
+        get_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (get_range(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS)
+        return fail(MG_ERR_INVALID, "pointer is not device memory");
+    cudaIpcMemHandle_t h;
+    MG_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    std::memset(handle, 0, sizeof(*handle));
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *offset = (uint64_t)((CUdeviceptr)dev_ptr - base);
+    return MG_OK;
+}
+
+mg_status mg_ipc_import(const mg_ipc_handle* handle, uint64_t offset, void** dev_ptr)
+{
+    g_last_error.clear();
+    if (!handle || !dev_ptr) return fail(MG_ERR_INVALID, "NULL argument");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    void* base = nullptr;
+    MG_CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    *dev_ptr = static_cast<uint8_t*>(base) + offset;
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto& m : g_ipc_maps) {
+        if (!m.user) {
+            m.user = *dev_ptr;
+            m.base = base;
+            return MG_OK;
+        }
+    }
+    cudaIpcCloseMemHandle(base);
+    *dev_ptr = nullptr;
+    return fail(MG_ERR_UNSUPPORTED, "too many imported buffers");
+}
+
+mg_status mg_ipc_close(void* dev_ptr)
+{
+    g_last_error.clear();
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (auto& m : g_ipc_maps) {
+        if (m.user == dev_ptr && dev_ptr) {
+            void* base = m.base;
+            m.user = m.base = nullptr;
+            MG_CUDA_TRY(cudaIpcCloseMemHandle(base));
+            return MG_OK;
+        }
+    }
+    return fail(MG_ERR_INVALID, "pointer was not returned by mg_ipc_import");
 }
 
 void mg_set_allocator(mg_alloc_fn alloc_fn, mg_free_fn free_fn, void* ctx)

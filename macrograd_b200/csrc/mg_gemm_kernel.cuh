@@ -72,6 +72,7 @@ constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
 constexpr int kThreads = 14 * 32;
 constexpr int kMaxBatchDims = 6;
+constexpr int kMaxPeers = 8;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
 constexpr uint32_t kSleepHintNs = 20000u;          // try_wait suspend hint
@@ -117,6 +118,12 @@ struct GemmParams {
     float alpha, beta;
     int epi;
     int* status;                // device status word pair {code, detail}
+    // Fused all-gather of a row-sharded GEMM: when npeers > 0, every output
+    // row chunk is written to each peers[q] (the full C of every rank, this
+    // rank's own included) at row peer_row0 + m instead of to C.
+    int npeers;
+    int64_t peer_row0;
+    float* peers[kMaxPeers];
 };
 
 struct TileCoord {
@@ -152,6 +159,8 @@ __device__ __forceinline__ void batch_index(int b, const GemmParams& p, int* idx
     }
 }
 
+constexpr int kSharedStateBytes = 512;   // SharedState, padded; the epilogue staging blocks follow
+
 struct SharedState {
     uint64_t full[kMaxStages];        // local: TMA landed
     uint64_t split_done[kMaxStages];  // MMA issuer's CTA: stage ready in every CTA
@@ -164,6 +173,8 @@ struct SharedState {
     uint32_t tmem_base;
     volatile int abort_flag;
 };
+
+static_assert(sizeof(SharedState) <= kSharedStateBytes, "SharedState outgrew its slot");
 
 __device__ __forceinline__ void record_failure(const GemmParams& p, SharedState* ss, int where)
 {
@@ -231,22 +242,56 @@ __device__ __forceinline__ uint32_t split_lo(uint32_t x)
     return d == d ? __float_as_uint(d) : 0u;
 }
 
-__device__ __forceinline__ void store_row_chunk(float* crow, int gn0, int nvalid, const float* v)
+constexpr int kStageFloatsPerWarp = 32 * 32;   // epilogue staging block per warp
+
+// Warp-collective store of a 32 x 32 output block. The TMEM layout gives each
+// lane one row (v[j] = column gn0 + j of row gm); written as is, one warp
+// store touches 32 rows at 16 bytes each, which is expensive over NVLink. The
+// block is therefore staged in shared memory (16-byte chunks XOR-swizzled by
+// row: conflict-free both ways) and written back row-contiguous: each warp
+// store covers 4 rows x 128 bytes. Destinations: C, or with a fused
+// all-gather every rank's full C. All 32 lanes must call it.
+__device__ __forceinline__ void store_block_out(const GemmParams& p, float* stage, const float* v, bool rok,
+                                                float* crow, int64_t coff, int gm, int gn0, int nvalid)
 {
-    if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(crow + gn0) & 15u) == 0)) {
-        float4* dst = reinterpret_cast<float4*>(crow + gn0);
+    const int lane = threadIdx.x & 31;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
+    for (int q = 0; q < 8; ++q)
+        reinterpret_cast<float4*>(stage + lane * 32)[q ^ (lane & 7)] =
+            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    __syncwarp();
+    const int ndst = p.npeers > 0 ? p.npeers : 1;
+    const int64_t peer_off = coff + (p.peer_row0 + gm) * p.ldc;
+#pragma unroll 1
+    for (int dsti = 0; dsti < ndst; ++dsti) {
+        // this lane's row start in the destination
+        float* mine = p.npeers > 0 ? p.peers[dsti] + peer_off : crow;
+        const int q = lane & 7;
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (j < nvalid) crow[gn0 + j] = v[j];
+        for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3);
+            const float4 val = reinterpret_cast<const float4*>(stage + r * 32)[q ^ (r & 7)];
+            float* row = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(mine), r));
+            const bool ok = __shfl_sync(0xffffffffu, rok ? 1 : 0, r) != 0;
+            if (!ok || 4 * q >= nvalid) continue;
+            float* dst = row + gn0 + 4 * q;
+            if (4 * q + 4 <= nvalid && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+                *reinterpret_cast<float4*>(dst) = val;
+            } else {
+                const float e[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (4 * q + j < nvalid) dst[j] = e[j];
+            }
+        }
     }
+    __syncwarp();
 }
 
 // tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
 // tmBlo map their lo planes (same layout), which the producer loads next to
 // the raw tiles instead of the split warps computing them.
+
 template <int BN, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     mg_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -505,6 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem_base + ((uint32_t)(sub * 32) << 16);
         const uint32_t t_part = lane_base + (uint32_t)(half * kHalf);
         const uint32_t t_master = lane_base + (uint32_t)(BN + half * kHalf);
+        float* stage_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes) +
+                         warp * kStageFloatsPerWarp;                  // this warp's store staging block
         const bool has_bias = (p.epi & kEpiBias) != 0;
         const bool softmax = (p.epi & kEpiSoftmax) != 0;
         uint32_t chunk_phase = 0;
@@ -622,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (causal && gn > gm) x = -INFINITY;
                             v[j] = expf(x - mx) / sum;
                         }
-                        if (rok) store_row_chunk(crow, c, min(32, p.N - c), v);
+                        store_block_out(p, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
                     }
                     tc_fence_before();
                     mbar_arrive(smem_u32(&ss->master_free));
@@ -633,27 +680,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (gn0 >= p.N) break;   // uniform across the warp
                     uint32_t r[32];
                     tmem_ld32(t_row + c, r);
-                    if (rok) {
-                        const int nvalid = min(32, p.N - gn0);
-                        float v[32];
+                    const int nvalid = min(32, p.N - gn0);
+                    float v[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
-                        if (has_bias) {
+                    for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+                    if (rok && has_bias) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (j < nvalid) v[j] += brow[(int64_t)(gn0 + j) * p.bias_cs];
-                        }
-                        if (p.beta != 0.f) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
-                        }
-                        store_row_chunk(crow, gn0, nvalid, v);
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nvalid) v[j] += brow[(int64_t)(gn0 + j) * p.bias_cs];
                     }
+                    if (rok && p.beta != 0.f) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
+                    }
+                    store_block_out(p, stage_w, v, rok, crow, coff, gm, gn0, nvalid);
                 }
             }
             tc_fence_before();
         }
+        // remote rows (fused all-gather) are visible system-wide before the
+        // kernel is seen as complete
+        if (p.npeers > 0) __threadfence_system();
     }
 
     tc_fence_before();

@@ -4,11 +4,14 @@ C = A @ B where the rows of A (and so of C) are split over the ranks and B is
 replicated. Rows of C depend only on the same rows of A, so each rank's GEMM is
 independent -- no collective inside the GEMM. When the caller needs the whole C
 on every device, the row blocks are all-gathered (NCCL over NVLink on GPUs,
-gloo on CPU in the tests). The reference has no multi-device path; this is the
-batch/row-sharded layer its matmul path gains here.
+gloo on CPU in the tests), or -- the B200 path -- written by each rank's GEMM
+epilogue directly into every rank's C over NVLink peer mappings (PeerRows +
+scatter_matmul), so the exchange overlaps the math. The reference has no
+multi-device path; this is the row-sharded layer its matmul path gains here.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional, Tuple
 
 import torch
@@ -48,6 +51,63 @@ def gather_rows(full: torch.Tensor, local: torch.Tensor, group=None) -> torch.Te
                 full[a:b] = got[: b - a]
     assert sizes[rank][1] - sizes[rank][0] == local.shape[0]
     return full
+
+
+class PeerRows:
+    """Every rank's full-C buffer, mapped into this process (CUDA IPC over
+    NVLink), in rank order -- the destinations of the fused all-gather.
+    Collective: every rank constructs it with its own `full` buffer."""
+
+    def __init__(self, full: torch.Tensor, group=None):
+        from . import _lib
+
+        self._lib = _lib.load()
+        self.group = group
+        self.full = full
+        rank = dist.get_rank(group)
+        world = dist.get_world_size(group)
+        handle = ctypes.create_string_buffer(64)
+        offset = ctypes.c_uint64(0)
+        _lib.check(self._lib.mg_ipc_export(ctypes.c_void_p(full.data_ptr()), handle, ctypes.byref(offset)))
+        mine = (bytes(handle.raw), int(offset.value))
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+        self.ptrs = []
+        self._imported = []
+        for r, (h, off) in enumerate(everyone):
+            if r == rank:
+                self.ptrs.append(full.data_ptr())
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(self._lib.mg_ipc_import(h, off, ctypes.byref(p)))
+            self.ptrs.append(p.value)
+            self._imported.append(p.value)
+        self.array = (ctypes.c_void_p * len(self.ptrs))(*self.ptrs)
+
+    def close(self):
+        """Unmap the peers' buffers (after every rank has stopped writing)."""
+        for p in self._imported:
+            self._lib.mg_ipc_close(ctypes.c_void_p(p))
+        self._imported = []
+
+
+def scatter_matmul(A_local: torch.Tensor, B: torch.Tensor, peers: PeerRows, row0: int,
+                   stream: Optional[torch.cuda.Stream] = None) -> None:
+    """This rank's rows of C = A @ B, written by the GEMM epilogue straight into
+    every rank's full C (all-gather fused into the kernel, mg_gemm_scatter_rows).
+    The caller orders it across ranks before C is read."""
+    from . import _lib
+
+    lib = _lib.load()
+    M, K = A_local.shape
+    N = B.shape[1]
+    d = _lib.GemmDesc()
+    lib.mg_gemm_desc_init(ctypes.byref(d), M, N, K, 0, 0)
+    d.ldc = peers.full.stride(0)
+    s = stream if stream is not None else torch.cuda.current_stream(A_local.device)
+    _lib.check(lib.mg_gemm_scatter_rows(ctypes.byref(d), ctypes.c_void_p(A_local.data_ptr()),
+                                        ctypes.c_void_p(B.data_ptr()), None, peers.array, len(peers.ptrs),
+                                        int(row0), ctypes.c_void_p(s.cuda_stream)))
 
 
 def sharded_matmul(A_local: torch.Tensor, B: torch.Tensor, full_out: Optional[torch.Tensor] = None,

@@ -1,0 +1,96 @@
+"""Row-sharded GEMM on 2 GPUs (one process each, NCCL): the all-gather fused
+into the GEMM epilogue (peer stores over NVLink) and the NCCL all-gather both
+leave the full C on every GPU, matching the oracle on sampled rows of each
+rank's block. Skipped when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle_bridge as ob
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, n, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        from macrograd_b200 import _lib, load
+        from macrograd_b200.sharded import PeerRows, row_block, scatter_matmul, sharded_matmul
+
+        lib = load()
+        A = ob.seeded_uniform((n, n // 2), 4)
+        B = ob.seeded_uniform((n // 2, n), 1004)
+        r0, r1 = row_block(n, world, rank)
+        A_local = torch.from_numpy(A[r0:r1].copy()).to(dev)
+        Bg = torch.from_numpy(B).to(dev)
+        report = {}
+        for mode in (_lib.MG_MODE_TF32X3, _lib.MG_MODE_TF32):
+            lib.mg_set_mode(mode)
+            full = torch.full((n, n), float("nan"), device=dev)
+            peers = PeerRows(full)
+            for _ in range(2):                       # two calls in a row into the same buffers
+                scatter_matmul(A_local, Bg, peers, r0)
+                fence = torch.zeros(1, device=dev)
+                dist.all_reduce(fence)                # every rank's kernel (and its remote rows) done
+            torch.cuda.synchronize()
+            full_nccl = torch.empty((n, n), device=dev)
+            sharded_matmul(A_local, Bg, full_out=full_nccl)
+            torch.cuda.synchronize()
+            got = full.cpu().numpy()
+            rows = [0, 5, n // 2 - 1, n // 2, n // 2 + 7, n - 1]
+            ref = ob.oracle_matmul(A[rows], B)
+            tol = 1e-5 if mode == _lib.MG_MODE_TF32X3 else 2e-3
+            report[mode] = (bool(np.all(np.isfinite(got))), ob.frob_rel_err(got[rows], ref) <= tol,
+                            bool(np.array_equal(got, full_nccl.cpu().numpy())))
+            dist.barrier()
+            peers.close()
+        q.put((rank, report))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_fused_all_gather_on_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, 1024, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    for rank, rep in results.items():
+        assert isinstance(rep, dict), f"rank {rank}: {rep}"
+        for mode, (finite, close, same) in rep.items():
+            assert finite, f"rank {rank} mode {mode}: C has rows nobody wrote"
+            assert close, f"rank {rank} mode {mode}: rows differ from the oracle"
+            assert same, f"rank {rank} mode {mode}: fused and NCCL all-gather differ"
