@@ -137,11 +137,13 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
  * orders steps across ranks (e.g. a small NCCL all-reduce after the GEMM)
  * before reading a C that other ranks write into, or overwriting it again.
  * `d` describes this rank's GEMM (M = its rows); d->ldc is the row stride of
- * the full C buffers; beta must be 0. */
+ * the full C buffers, which have rows_full rows; beta must be 0. For a 2-D C
+ * the remote rows leave as TMA bulk tensor stores, so the copies run on the
+ * TMA engine while the warps go on. */
 #define MG_MAX_PEERS 8
 mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const float* B,
                                const float* bias, float* const* peer_C, int32_t npeers,
-                               int64_t row0, void* stream);
+                               int64_t row0, int64_t rows_full, void* stream);
 
 /* CUDA IPC plumbing for peer_C: export a device buffer of this process
  * (a handle plus the buffer's offset inside its allocation), and map a buffer

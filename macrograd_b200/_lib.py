@@ -84,7 +84,7 @@ SIGNATURES = {
                                          ctypes.c_float, _I32, _P]),
     "mg_matmul_noalloc": (ctypes.c_int, [_P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
     "mg_gemm_scatter_rows": (ctypes.c_int, [ctypes.POINTER(GemmDesc), _P, _P, _P, ctypes.POINTER(_P), _I32,
-                                            ctypes.c_int64, _P]),
+                                            ctypes.c_int64, ctypes.c_int64, _P]),
     "mg_ipc_export": (ctypes.c_int, [_P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64)]),
     "mg_ipc_import": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(_P)]),
     "mg_ipc_close": (ctypes.c_int, [_P]),

@@ -409,7 +409,7 @@ mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace&
 
 template <int BN, bool kPair>
 mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& malo,
-                    const CUtensorMap& mblo, mg::GemmParams& gp, cudaStream_t st)
+                    const CUtensorMap& mblo, mg::GemmParams& gp, const mg::PeerMaps& pm, cudaStream_t st)
 {
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
@@ -449,10 +449,10 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         }
         const int pairs = std::max(1, std::min(gp.total_tiles, dev->max_clusters[slot - 3]));
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp));
+        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm));
     } else {
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
-        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, gp);
+        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, gp, pm);
         MG_CUDA_TRY(cudaGetLastError());
     }
     g_launches++;
@@ -563,6 +563,7 @@ void mg_gemm_desc_init(mg_gemm_desc* d, int32_t M, int32_t N, int32_t K, int32_t
 struct ScatterSpec {
     int npeers;
     int64_t row0;
+    int64_t rows_full;          // rows of every rank's full C
     float* peers[mg::kMaxPeers];
 };
 
@@ -729,23 +730,42 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.beta = d->beta;
     gp.epi = d->epilogue;
     gp.status = dev->status;
+    mg::PeerMaps pm;
+    std::memset(&pm, 0, sizeof(pm));
     if (scatter) {
         gp.npeers = scatter->npeers;
         gp.peer_row0 = scatter->row0;
         for (int q = 0; q < scatter->npeers; ++q) gp.peers[q] = scatter->peers[q];
+        // TMA bulk stores need a 2-D C with 16-byte aligned rows in every destination
+        bool tma_ok = nbd == 0 && (d->ldc * 4) % 16 == 0 && scatter->rows_full < (1ll << 31);
+        for (int q = 0; q < scatter->npeers; ++q)
+            tma_ok = tma_ok && (reinterpret_cast<uintptr_t>(scatter->peers[q]) & 15u) == 0;
+        if (tma_ok) {
+            for (int q = 0; q < scatter->npeers; ++q) {
+                cuuint64_t dims[2] = {(cuuint64_t)d->N, (cuuint64_t)scatter->rows_full};
+                cuuint64_t strides[1] = {(cuuint64_t)(d->ldc * 4)};
+                cuuint32_t box[2] = {32, 32};
+                cuuint32_t estr[2] = {1, 1};
+                CUresult r = g_encode(&pm.m[q], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, scatter->peers[q], dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                if (r != CUDA_SUCCESS) return fail(MG_ERR_CUDA, "tensor map of peer C %d failed (%d)", q, (int)r);
+            }
+            gp.peer_tma = 1;
+        }
     }
 
     if (pair) {
         switch (bn) {
-        case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, st);
-        case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, st);
-        default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, st);
+        case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, pm, st);
+        case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, pm, st);
+        default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, pm, st);
         }
     }
     switch (bn) {
-    case 64: return launch_tc<64, false>(dev, ma, mb, malo, mblo, gp, st);
-    case 128: return launch_tc<128, false>(dev, ma, mb, malo, mblo, gp, st);
-    default: return launch_tc<256, false>(dev, ma, mb, malo, mblo, gp, st);
+    case 64: return launch_tc<64, false>(dev, ma, mb, malo, mblo, gp, pm, st);
+    case 128: return launch_tc<128, false>(dev, ma, mb, malo, mblo, gp, pm, st);
+    default: return launch_tc<256, false>(dev, ma, mb, malo, mblo, gp, pm, st);
     }
 }
 
@@ -884,18 +904,22 @@ mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const in
 }
 
 mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const float* B, const float* bias,
-                               float* const* peer_C, int32_t npeers, int64_t row0, void* stream)
+                               float* const* peer_C, int32_t npeers, int64_t row0, int64_t rows_full,
+                               void* stream)
 {
     g_last_error.clear();
     if (!d) return fail(MG_ERR_INVALID, "descriptor is NULL");
     if (npeers < 1 || npeers > mg::kMaxPeers)
         return fail(MG_ERR_INVALID, "npeers %d outside [1, %d]", npeers, mg::kMaxPeers);
     if (!peer_C) return fail(MG_ERR_INVALID, "peer_C is NULL");
-    if (row0 < 0) return fail(MG_ERR_INVALID, "negative row offset");
+    if (row0 < 0 || row0 + d->M > rows_full)
+        return fail(MG_ERR_INVALID, "rows [%lld, %lld) are not inside the %lld rows of the full C",
+                    (long long)row0, (long long)(row0 + d->M), (long long)rows_full);
     if (d->beta != 0.f) return fail(MG_ERR_INVALID, "the scattering GEMM does not accumulate (beta must be 0)");
     ScatterSpec sc;
     sc.npeers = npeers;
     sc.row0 = row0;
+    sc.rows_full = rows_full;
     for (int q = 0; q < npeers; ++q) {
         if (!peer_C[q]) return fail(MG_ERR_INVALID, "peer_C[%d] is NULL", q);
         sc.peers[q] = peer_C[q];

@@ -123,7 +123,13 @@ struct GemmParams {
     // rank's own included) at row peer_row0 + m instead of to C.
     int npeers;
     int64_t peer_row0;
+    int peer_tma;               // full 32-row blocks go out as TMA bulk stores (PeerMaps)
     float* peers[kMaxPeers];
+};
+
+// 2-D tensor maps over every rank's full C (fused all-gather with TMA stores).
+struct PeerMaps {
+    CUtensorMap m[kMaxPeers];
 };
 
 struct TileCoord {
@@ -159,7 +165,8 @@ __device__ __forceinline__ void batch_index(int b, const GemmParams& p, int* idx
     }
 }
 
-constexpr int kSharedStateBytes = 512;   // SharedState, padded; the epilogue staging blocks follow
+constexpr int kSharedStateBytes = 1024;  // SharedState, padded; the epilogue staging blocks follow
+                                         // (1024-byte aligned: TMA stores read them 128B-swizzled)
 
 struct SharedState {
     uint64_t full[kMaxStages];        // local: TMA landed
@@ -251,8 +258,9 @@ constexpr int kStageFloatsPerWarp = 32 * 32;   // epilogue staging block per war
 // row: conflict-free both ways) and written back row-contiguous: each warp
 // store covers 4 rows x 128 bytes. Destinations: C, or with a fused
 // all-gather every rank's full C. All 32 lanes must call it.
-__device__ __forceinline__ void store_block_out(const GemmParams& p, float* stage, const float* v, bool rok,
-                                                float* crow, int64_t coff, int gm, int gn0, int nvalid)
+__device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerMaps& pm, float* stage,
+                                                const float* v, bool rok, float* crow, int64_t coff, int gm,
+                                                int gn0, int nvalid)
 {
     const int lane = threadIdx.x & 31;
 #pragma unroll
@@ -260,6 +268,23 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, float* stag
         reinterpret_cast<float4*>(stage + lane * 32)[q ^ (lane & 7)] =
             make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     __syncwarp();
+    const int block_row0 = gm - lane;   // first row of this warp's 32-row block
+    if (p.npeers > 0 && p.peer_tma && block_row0 + 32 <= p.M) {
+        // The staging block is laid out as a TMA 128B-swizzled {32, 32} box:
+        // hand it to the TMA engine once per destination (columns past N are
+        // clipped by the map), and wait only until it has been read.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            const uint32_t src = smem_u32(stage);
+            for (int q = 0; q < p.npeers; ++q)
+                tma_store_2d(&pm.m[q], src, gn0, (int32_t)(p.peer_row0 + block_row0));
+            bulk_commit_group();
+            bulk_wait_read_all();
+        }
+        __syncwarp();
+        return;
+    }
     const int ndst = p.npeers > 0 ? p.npeers : 1;
     const int64_t peer_off = coff + (p.peer_row0 + gm) * p.ldc;
 #pragma unroll 1
@@ -298,7 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo,
                       const __grid_constant__ CUtensorMap tmBlo,
-                      const __grid_constant__ GemmParams p)
+                      const __grid_constant__ GemmParams p,
+                      const __grid_constant__ PeerMaps pm)
 {
     using L = Layout<BN, kPair>;
     extern __shared__ uint8_t smem_raw[];
@@ -669,7 +695,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             if (causal && gn > gm) x = -INFINITY;
                             v[j] = expf(x - mx) / sum;
                         }
-                        store_block_out(p, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
+                        store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
                     }
                     tc_fence_before();
                     mbar_arrive(smem_u32(&ss->master_free));
@@ -694,14 +720,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j)
                             if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
                     }
-                    store_block_out(p, stage_w, v, rok, crow, coff, gm, gn0, nvalid);
+                    store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, gn0, nvalid);
                 }
             }
             tc_fence_before();
         }
-        // remote rows (fused all-gather) are visible system-wide before the
-        // kernel is seen as complete
-        if (p.npeers > 0) __threadfence_system();
+        // remote rows (fused all-gather) have landed and are visible
+        // system-wide before the kernel is seen as complete
+        if (p.npeers > 0) {
+            if (lane == 0) bulk_wait_all();
+            __syncwarp();
+            __threadfence_system();
+        }
     }
 
     tc_fence_before();

@@ -107,7 +107,7 @@ def scatter_matmul(A_local: torch.Tensor, B: torch.Tensor, peers: PeerRows, row0
     s = stream if stream is not None else torch.cuda.current_stream(A_local.device)
     _lib.check(lib.mg_gemm_scatter_rows(ctypes.byref(d), ctypes.c_void_p(A_local.data_ptr()),
                                         ctypes.c_void_p(B.data_ptr()), None, peers.array, len(peers.ptrs),
-                                        int(row0), ctypes.c_void_p(s.cuda_stream)))
+                                        int(row0), int(peers.full.shape[0]), ctypes.c_void_p(s.cuda_stream)))
 
 
 def sharded_matmul(A_local: torch.Tensor, B: torch.Tensor, full_out: Optional[torch.Tensor] = None,
