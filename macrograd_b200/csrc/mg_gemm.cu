@@ -46,8 +46,8 @@ struct DeviceState {
     bool ready = false;
     int sm_count = 0;
     int max_smem = 0;
-    size_t attr_smem[6] = {0, 0, 0, 0, 0, 0};   // dynamic smem opted in, per kernel variant
-    int max_clusters[3] = {0, 0, 0};            // resident CTA pairs, per pair-kernel tile width
+    size_t attr_smem[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // dynamic smem opted in, per kernel variant
+    int max_clusters[4] = {0, 0, 0, 0};               // resident CTA pairs, per pair-kernel tile width
     int* status = nullptr;   // device address of g_device_status
 };
 DeviceState g_dev[kMaxDevices];
@@ -59,8 +59,22 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 struct IpcMap {
     void* user = nullptr;
     void* base = nullptr;
+    size_t size = 0;            // of the mapped allocation (0: unknown)
 };
 IpcMap g_ipc_maps[64];
+
+// Whether p lies in a buffer mapped from another process by mg_ipc_import.
+bool ipc_imported(const void* p)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    for (const auto& m : g_ipc_maps) {
+        if (!m.user) continue;
+        const uintptr_t b = reinterpret_cast<uintptr_t>(m.base);
+        if (m.size ? (a >= b && a < b + m.size) : p == m.user) return true;
+    }
+    return false;
+}
 
 mg_status fail(mg_status s, const char* fmt, ...)
 {
@@ -99,7 +113,7 @@ constexpr auto kernel_of()
     return &mg::mg_gemm_tc_kernel<BN, kPair>;
 }
 
-int bn_slot(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : 2); }
+int bn_slot(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : (bn == 224 ? 3 : 2)); }
 
 mg_status device_state(DeviceState** out)
 {
@@ -415,14 +429,28 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     const int split = gp.split;
     // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
     const size_t fixed = 1024 + mg::kSharedStateBytes + (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4 + 64;
-    const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);
-    int stages = (int)((size_t)(dev->max_smem - (int)fixed) / per_stage);
+    const size_t avail = (size_t)dev->max_smem - fixed;
+    const size_t sb = L::kStageBytes;
+    // 3xTF32: the lo tiles live in their own short ring (the split fills a slot
+    // just before its MMAs), so more shared memory goes to raw stages -- the
+    // TMA look-ahead. Pre-split lo planes arrive with their stage (tied).
+    int stages;
+    if (!split) {
+        stages = (int)(avail / sb);
+        gp.lo_slots = 0;
+    } else if (gp.lo_tied) {
+        stages = (int)(avail / (2 * sb));
+        gp.lo_slots = stages;
+    } else {
+        stages = (int)((avail - std::min(avail, (size_t)gp.lo_slots * sb)) / sb);
+    }
     stages = std::min(stages, mg::kMaxStages);
     if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
+    if (split && gp.lo_tied) gp.lo_slots = stages;
     gp.stages = stages;
-    const size_t smem = fixed + per_stage * stages;
+    const size_t smem = fixed + sb * (size_t)(stages + (split ? gp.lo_slots : 0));
     auto k = kernel_of<BN, kPair>();
-    const int slot = bn_slot(BN) + (kPair ? 3 : 0);
+    const int slot = bn_slot(BN) + (kPair ? 4 : 0);
     if (dev->attr_smem[slot] < smem) {
         MG_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         dev->attr_smem[slot] = smem;
@@ -441,13 +469,13 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (dev->max_clusters[slot - 3] == 0) {
+        if (dev->max_clusters[slot - 4] == 0) {
             cfg.gridDim = dim3((unsigned)dev->sm_count, 1, 1);
             int n = 0;
             MG_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, k, &cfg));
-            dev->max_clusters[slot - 3] = std::max(1, std::min(n, dev->sm_count / 2));
+            dev->max_clusters[slot - 4] = std::max(1, std::min(n, dev->sm_count / 2));
         }
-        const int pairs = std::max(1, std::min(gp.total_tiles, dev->max_clusters[slot - 3]));
+        const int pairs = std::max(1, std::min(gp.total_tiles, dev->max_clusters[slot - 4]));
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
         MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm));
     } else {
@@ -493,6 +521,26 @@ bool want_presplit(double flops, int64_t m_tiles, int64_t n_tiles)
 
 // Pair kernel (two SMs per 256-row tile) when a batch has more than 128 rows;
 // MG_GEMM_PAIR=0 / =1 forces the single-SM / pair kernel (tests, tuning).
+// Output tile width. Pair tiles may be 224 wide instead of 256 when that
+// takes fewer waves over the SM pairs. A K-block costs the pipeline about the
+// same time at either width (its hand-offs, not the MMAs, set the pace), so
+// only the wave count counts and 256 wins ties.
+int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, const DeviceState* dev)
+{
+    const int forced = tuning_int("MG_GEMM_BN", 0, 64, 256);
+    const bool fits = !(d->epilogue & MG_EPI_SOFTMAX) || d->N <= forced;   // softmax: one tile per row
+    if (fits && (forced == 64 || forced == 128 || forced == 256 || (forced == 224 && pair))) return forced;
+    const int base = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
+    if (!pair || base != 256 || (d->epilogue & MG_EPI_SOFTMAX)) return base;
+    const int64_t m_tiles = (d->M + 2 * mg::kBM - 1) / (2 * mg::kBM);
+    const int64_t units = std::max(1, dev->sm_count / 2);
+    auto cost = [&](int bn) {
+        const int64_t tiles = nbatch * m_tiles * ((d->N + bn - 1) / bn);
+        return (tiles + units - 1) / units;   // waves
+    };
+    return cost(224) < cost(256) ? 224 : 256;
+}
+
 bool use_pair(int M)
 {
     if (const char* e = std::getenv("MG_GEMM_PAIR")) {
@@ -650,8 +698,8 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
             return fail(MG_ERR_UNSUPPORTED, "operand B cannot be mapped for TMA");
     }
 
-    const int bn = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
     const bool pair = use_pair(d->M);
+    const int bn = choose_bn(d, pair, nbatch, dev);
     const int tile_rows = pair ? 2 * mg::kBM : mg::kBM;   // output rows per tile
     const int b_rows = pair ? bn / 2 : bn;                // B rows (N) one CTA loads
 
@@ -704,6 +752,9 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);
     gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
     gp.presplit = presplit ? 1 : 0;
+    gp.lo_tied = (presplit || !tuning_int("MG_GEMM_LO_RING", 0, 0, 1)) ? 1 : 0;
+    gp.lo_slots = tuning_int("MG_GEMM_LO_SLOTS", 2, 1, 4);
+    gp.elect = tuning_int("MG_GEMM_ELECT", 0, 0, 2);
     gp.a_mn = a_mn;
     gp.b_mn = b_mn;
     gp.a_rank = 2 + am.nmap;
@@ -732,7 +783,27 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.status = dev->status;
     mg::PeerMaps pm;
     std::memset(&pm, 0, sizeof(pm));
-    if (scatter) {
+    // Export mode (default): the epilogue writes this GPU's own full C and the
+    // kernel's export warps copy each finished tile to the other ranks, so the
+    // epilogue never waits on NVLink. Needs one destination in this process's
+    // own memory (not mapped from another rank).
+    int local = -1;
+    if (scatter && tuning_int("MG_GEMM_EXPORT", 1, 0, 1)) {
+        for (int q = 0; q < scatter->npeers && local < 0; ++q)
+            if (!ipc_imported(scatter->peers[q])) local = q;
+    }
+    if (scatter && local >= 0) {
+        gp.C = scatter->peers[local];
+        gp.peer_row0 = scatter->row0;
+        gp.export_peers = 1;
+        bool vec = d->N % 4 == 0 && d->ldc % 4 == 0;
+        for (int i = 0; i < nbd; ++i) vec = vec && d->c_batch_stride[i] % 4 == 0;
+        for (int q = 0; q < scatter->npeers; ++q) {
+            vec = vec && (reinterpret_cast<uintptr_t>(scatter->peers[q]) & 15u) == 0;
+            if (q != local) gp.peers[gp.npeers++] = scatter->peers[q];
+        }
+        gp.export_vec = vec ? 1 : 0;
+    } else if (scatter) {
         gp.npeers = scatter->npeers;
         gp.peer_row0 = scatter->row0;
         for (int q = 0; q < scatter->npeers; ++q) gp.peers[q] = scatter->peers[q];
@@ -759,6 +830,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
         switch (bn) {
         case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, pm, st);
         case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, pm, st);
+        case 224: return launch_tc<224, true>(dev, ma, mb, malo, mblo, gp, pm, st);
         default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, pm, st);
         }
     }
@@ -930,10 +1002,9 @@ mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const floa
 
 static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(mg_ipc_handle), "IPC handle does not fit");
 
-mg_status mg_ipc_export(const void* dev_ptr, mg_ipc_handle* handle, uint64_t* offset)
+// The allocation containing a device pointer (driver cuMemGetAddressRange).
+static mg_status address_range(const void* p, CUdeviceptr* base, size_t* size)
 {
-    g_last_error.clear();
-    if (!dev_ptr || !handle || !offset) return fail(MG_ERR_INVALID, "NULL argument");
     static PFN_cuMemGetAddressRange_v3020 get_range = nullptr;
     if (!get_range) {
         void* fn = nullptr;
@@ -942,10 +1013,19 @@ mg_status mg_ipc_export(const void* dev_ptr, mg_ipc_handle* handle, uint64_t* of
         if (q != cudaDriverEntryPointSuccess || !fn) return fail(MG_ERR_CUDA, "cuMemGetAddressRange unavailable");
         get_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
     }
+    if (get_range(base, size, (CUdeviceptr)p) != CUDA_SUCCESS)
+        return fail(MG_ERR_INVALID, "pointer is not device memory");
+    return MG_OK;
+}
+
+mg_status mg_ipc_export(const void* dev_ptr, mg_ipc_handle* handle, uint64_t* offset)
+{
+    g_last_error.clear();
+    if (!dev_ptr || !handle || !offset) return fail(MG_ERR_INVALID, "NULL argument");
     CUdeviceptr base = 0;
     size_t size = 0;
-    if (get_range(&base, &size, (CUdeviceptr)dev_ptr) != CUDA_SUCCESS)
-        return fail(MG_ERR_INVALID, "pointer is not device memory");
+    mg_status s = address_range(dev_ptr, &base, &size);
+    if (s != MG_OK) return s;
     cudaIpcMemHandle_t h;
     MG_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
     std::memset(handle, 0, sizeof(*handle));
@@ -963,11 +1043,16 @@ mg_status mg_ipc_import(const mg_ipc_handle* handle, uint64_t offset, void** dev
     void* base = nullptr;
     MG_CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
     *dev_ptr = static_cast<uint8_t*>(base) + offset;
+    CUdeviceptr rb = 0;
+    size_t rsize = 0;
+    if (address_range(base, &rb, &rsize) != MG_OK || rb != (CUdeviceptr)base) rsize = 0;
+    g_last_error.clear();
     std::lock_guard<std::mutex> lk(g_mu);
     for (auto& m : g_ipc_maps) {
         if (!m.user) {
             m.user = *dev_ptr;
             m.base = base;
+            m.size = rsize;
             return MG_OK;
         }
     }
@@ -984,6 +1069,7 @@ mg_status mg_ipc_close(void* dev_ptr)
         if (m.user == dev_ptr && dev_ptr) {
             void* base = m.base;
             m.user = m.base = nullptr;
+            m.size = 0;
             MG_CUDA_TRY(cudaIpcCloseMemHandle(base));
             return MG_OK;
         }

@@ -25,7 +25,7 @@
 //    *partial*, which the epilogue warps add into a TMEM *master* with fp32
 //    round-to-nearest adds; the error then no longer grows with K.
 //
-// Roles (448 threads = 14 warps per CTA, one CTA per SM):
+// Roles (512 threads = 16 warps per CTA, one CTA per SM):
 //   warps 0-7   epilogue: warp w owns TMEM lanes 32(w%4).. (tile rows) and the
 //               column half w/4. Per chunk: master (+)= partial. Per tile:
 //               alpha / bias / beta / store from the master; the row softmax
@@ -34,6 +34,9 @@
 //               they report the landed stage to the MMA issuer.
 //   warp 12     TMA producer (one lane), into this CTA's shared memory.
 //   warp 13     TMEM allocator; one lane (of the leader CTA) issues tcgen05.mma.
+//   warps 14-15 export (fused all-gather): once the epilogue has written a tile
+//               into this GPU's C, copy its rows into every peer's C over
+//               NVLink, so the epilogue never waits on the fabric.
 // TMEM: columns [0, BN) partial, [BN, 2BN) master.
 //
 // Operand layouts in shared memory (per stage, 1024-byte aligned):
@@ -70,7 +73,9 @@ constexpr int kSplitWarp0 = 8;
 constexpr int kSplitThreads = 128;
 constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
-constexpr int kThreads = 14 * 32;
+constexpr int kExportWarp0 = 14;
+constexpr int kExportThreads = 64;
+constexpr int kThreads = 16 * 32;
 constexpr int kMaxBatchDims = 6;
 constexpr int kMaxPeers = 8;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
@@ -87,7 +92,8 @@ enum : int {
     kWaitMmaStage = 4,
     kWaitEpiloguePartial = 5,
     kWaitEpilogueMaster = 6,
-    kWaitEpilogueMasterFree = 7
+    kWaitEpilogueMasterFree = 7,
+    kWaitExportTile = 8
 };
 
 struct GemmParams {
@@ -102,6 +108,9 @@ struct GemmParams {
     int relay_spin;             // split warps poll without suspend hints
     int split;                  // 1 = 3xTF32
     int presplit;               // 3xTF32 with lo planes precomputed in HBM (tmAlo / tmBlo)
+    int lo_slots;               // 3xTF32: lo tiles in shared memory (a ring, or one per stage)
+    int lo_tied;                // 1: lo slot = stage (freed with it); 0: separate ring of lo_slots
+    int elect;                  // split warps report a stage: 0 per thread, 1 per warp, 2 per CTA
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
     int a_rank, b_rank;         // tensor-map ranks (2 + mapped batch dims)
     uint32_t idesc;
@@ -121,9 +130,14 @@ struct GemmParams {
     // Fused all-gather of a row-sharded GEMM: when npeers > 0, every output
     // row chunk is written to each peers[q] (the full C of every rank, this
     // rank's own included) at row peer_row0 + m instead of to C.
+    // With export_peers the epilogue writes only C (this GPU's full C, at row
+    // peer_row0 + m) and the export warps copy each finished tile from there
+    // into peers[0..npeers) (the other ranks' full C).
     int npeers;
     int64_t peer_row0;
     int peer_tma;               // full 32-row blocks go out as TMA bulk stores (PeerMaps)
+    int export_peers;
+    int export_vec;             // N, ldc and every destination allow 16-byte copies
     float* peers[kMaxPeers];
 };
 
@@ -172,6 +186,7 @@ struct SharedState {
     uint64_t full[kMaxStages];        // local: TMA landed
     uint64_t split_done[kMaxStages];  // MMA issuer's CTA: stage ready in every CTA
     uint64_t empty[kMaxStages];       // local: the MMAs reading the stage are done
+    uint64_t lo_empty[kMaxStages];    // local: the MMAs reading the lo slot are done (lo ring)
     uint64_t part_full;               // local: partial accumulator complete
     uint64_t part_free;               // MMA issuer's CTA: every epilogue took the partial
     uint64_t master_done;             // local (softmax): every epilogue thread wrote its master half
@@ -179,6 +194,8 @@ struct SharedState {
     uint64_t drain;
     uint32_t tmem_base;
     volatile int abort_flag;
+    unsigned int tiles_stored;        // epilogue warps x tiles written to C (export mode)
+    unsigned int split_warps_done[kMaxStages];   // elect == 2: split warps through the stage
 };
 
 static_assert(sizeof(SharedState) <= kSharedStateBytes, "SharedState outgrew its slot");
@@ -231,14 +248,27 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity)
     }
 }
 
+__host__ __device__ constexpr uint32_t pow2_at_least(uint32_t x, uint32_t p = 32)
+{
+    return p >= x ? p : pow2_at_least(x, 2 * p);
+}
+
 template <int BN, bool kPair>
 struct Layout {
-    static constexpr int kBRows = kPair ? BN / 2 : BN;       // B rows (N) this CTA loads
+    static_assert(BN % 32 == 0 && (!kPair || BN % 32 == 0), "tile width must be a multiple of 32");
+    static constexpr int kBRows = kPair ? BN / 2 : BN;       // B rows (N) this CTA's MMA operand has
+    static constexpr int kBBoxes = (kBRows + 31) / 32;       // MN-major: 32-wide TMA boxes
     static constexpr uint32_t kABytes = kBM * 128;          // 16 KB
-    static constexpr uint32_t kBBytes = kBRows * 128;
+    static constexpr uint32_t kBBytes = kBBoxes * 32 * 128;  // room for whole MN-major boxes
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kTmemCols = 2 * BN;           // partial + master
+    static constexpr uint32_t kTmemCols = pow2_at_least(2 * BN);   // partial + master
     static constexpr int kTileRows = kPair ? 2 * kBM : kBM;  // output rows per tile
+    static constexpr int kChunks = BN / 32;                  // 32-column epilogue chunks
+    static constexpr int kHalfChunks = (kChunks + 1) / 2;    // chunks of column half 0
+    // bytes one stage's TMA loads deliver (K-major B: kBRows rows; MN-major:
+    // whole 32-wide boxes, the last one partly past this CTA's columns)
+    static constexpr uint32_t kLoadA = kABytes;
+    __host__ __device__ static constexpr uint32_t load_b(bool mn) { return mn ? kBBytes : (uint32_t)kBRows * 128u; }
 };
 
 // lo = x - hi of the 3xTF32 split, hi = x with its 13 low mantissa bits
@@ -250,6 +280,12 @@ __device__ __forceinline__ uint32_t split_lo(uint32_t x)
 }
 
 constexpr int kStageFloatsPerWarp = 32 * 32;   // epilogue staging block per warp
+
+// largest divisor of n that is at most 16 (16-byte loads a split thread keeps in flight)
+__host__ __device__ constexpr int batch_of(int n, int b = 16)
+{
+    return (b <= 1 || n % b == 0) ? (b < 1 ? 1 : b) : batch_of(n, b - 1);
+}
 
 // Warp-collective store of a 32 x 32 output block. The TMEM layout gives each
 // lane one row (v[j] = column gn0 + j of row gm); written as is, one warp
@@ -269,7 +305,8 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
             make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     __syncwarp();
     const int block_row0 = gm - lane;   // first row of this warp's 32-row block
-    if (p.npeers > 0 && p.peer_tma && block_row0 + 32 <= p.M) {
+    const bool to_peers = p.npeers > 0 && !p.export_peers;   // the epilogue itself writes every rank's C
+    if (to_peers && p.peer_tma && block_row0 + 32 <= p.M) {
         // The staging block is laid out as a TMA 128B-swizzled {32, 32} box:
         // hand it to the TMA engine once per destination (columns past N are
         // clipped by the map), and wait only until it has been read.
@@ -285,12 +322,12 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
         __syncwarp();
         return;
     }
-    const int ndst = p.npeers > 0 ? p.npeers : 1;
+    const int ndst = to_peers ? p.npeers : 1;
     const int64_t peer_off = coff + (p.peer_row0 + gm) * p.ldc;
 #pragma unroll 1
     for (int dsti = 0; dsti < ndst; ++dsti) {
         // this lane's row start in the destination
-        float* mine = p.npeers > 0 ? p.peers[dsti] + peer_off : crow;
+        float* mine = to_peers ? p.peers[dsti] + peer_off : crow;
         const int q = lane & 7;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -313,6 +350,79 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
     __syncwarp();
 }
 
+// Bounded wait until the shared counter reaches `target`.
+__device__ __forceinline__ bool wait_count(const unsigned int* ctr, unsigned int target, SharedState* ss,
+                                           const GemmParams& p, int where)
+{
+    const volatile unsigned int* c = ctr;
+    if (*c >= target) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        __nanosleep(1000);
+        if (*c >= target) return true;
+        if (ss->abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_failure(p, ss, where);
+            return false;
+        }
+    }
+}
+
+// Export of one finished tile (rows x cols of this CTA, already in this GPU's
+// C at src) to every peer's C at the same element offset: the export threads
+// read 16-byte pieces from L2 (ld.cg: the epilogue wrote them moments ago)
+// and store them over NVLink, kUnroll pieces in flight per thread.
+template <bool kVec>
+__device__ __forceinline__ void export_tile(const GemmParams& p, int64_t off, int rows, int cols, int et)
+{
+    constexpr int kUnroll = 8;
+    const float* src = p.C + off;
+    if (kVec) {
+        const int c4 = cols >> 2;
+        const int items = rows * c4;
+#pragma unroll 1
+        for (int base = et; base < items; base += kExportThreads * kUnroll) {
+            float4 v[kUnroll];
+            int64_t eo[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int i = base + u * kExportThreads;
+                const int r = i / c4;
+                eo[u] = (int64_t)r * p.ldc + 4 * (i - r * c4);
+                if (i < items) v[u] = __ldcg(reinterpret_cast<const float4*>(src + eo[u]));
+            }
+#pragma unroll 1
+            for (int q = 0; q < p.npeers; ++q) {
+                float* dst = p.peers[q] + off;
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u)
+                    if (base + u * kExportThreads < items) *reinterpret_cast<float4*>(dst + eo[u]) = v[u];
+            }
+        }
+    } else {
+        const int items = rows * cols;
+#pragma unroll 1
+        for (int base = et; base < items; base += kExportThreads * kUnroll) {
+            float v[kUnroll];
+            int64_t eo[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int i = base + u * kExportThreads;
+                const int r = i / cols;
+                eo[u] = (int64_t)r * p.ldc + (i - r * cols);
+                if (i < items) v[u] = __ldcg(src + eo[u]);
+            }
+#pragma unroll 1
+            for (int q = 0; q < p.npeers; ++q) {
+                float* dst = p.peers[q] + off;
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u)
+                    if (base + u * kExportThreads < items) dst[eo[u]] = v[u];
+            }
+        }
+    }
+}
+
 // tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
 // tmBlo map their lo planes (same layout), which the producer loads next to
 // the raw tiles instead of the split warps computing them.
@@ -333,13 +443,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const uint32_t smem_base = smem_u32(smem);
     const int stages = p.stages;
+    // shared memory: raw stages, then (3xTF32) the lo slots, then the barriers
     const uint32_t raw_region = (uint32_t)stages * L::kStageBytes;
-    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region * (p.split ? 2u : 1u));
+    const uint32_t lo_region = p.split ? (uint32_t)p.lo_slots * L::kStageBytes : 0u;
+    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region + lo_region);
 
     auto a_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes; };
     auto b_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes + L::kABytes; };
-    auto a_lo = [&](int s) { return a_raw(s) + raw_region; };
-    auto b_lo = [&](int s) { return b_raw(s) + raw_region; };
+    auto a_lo = [&](int l) { return smem_base + raw_region + (uint32_t)l * L::kStageBytes; };
+    auto b_lo = [&](int l) { return a_lo(l) + L::kABytes; };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -355,12 +467,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&ss->split_done[s]), kSplitThreads * (kPair ? 2 : 1));
             mbar_init(smem_u32(&ss->empty[s]), 1);
         }
+        for (int l = 0; l < kMaxStages; ++l) {
+            mbar_init(smem_u32(&ss->lo_empty[l]), 1);
+            ss->split_warps_done[l] = 0u;
+        }
         mbar_init(smem_u32(&ss->part_full), 1);
         mbar_init(smem_u32(&ss->part_free), kEpiThreads * (kPair ? 2 : 1));
         mbar_init(smem_u32(&ss->master_done), kEpiThreads);
         mbar_init(smem_u32(&ss->master_free), kEpiThreads / 2);
         mbar_init(smem_u32(&ss->drain), 1);
         ss->abort_flag = 0;
+        ss->tiles_stored = 0u;
         mbar_fence_init();
     }
     if (warp == kProducerWarp && lane == 0) {
@@ -422,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     const uint32_t fb = smem_u32(&ss->full[stage]);
-                    mbar_arrive_expect_tx(fb, L::kStageBytes * (p.presplit ? 2u : 1u));
+                    mbar_arrive_expect_tx(fb, (L::kLoadA + L::load_b(p.b_mn != 0)) * (p.presplit ? 2u : 1u));
                     const int k0 = kb * kBK;
                     // raw tiles, and in pre-split mode the lo tiles one region higher
                     for (int plane = 0; plane < (p.presplit ? 2 : 1); ++plane) {
@@ -441,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             tma_load(mb, fb, db, p.b_rank, k0, n0, b2, b3, b4);
                         } else {
 #pragma unroll
-                            for (int j = 0; j < L::kBRows / 32; ++j)
+                            for (int j = 0; j < L::kBBoxes; ++j)
                                 tma_load(mb, fb, db + 4096u * j, p.b_rank, n0 + 32 * j, k0, b2, b3, b4);
                         }
                     }
@@ -478,12 +595,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kPair) tc_commit_pair_all(bar, (uint16_t)0x3);
                 else tc_commit(bar);
             };
+            const bool lo_ring = split && !p.lo_tied;
             int stage = 0;
             uint32_t phase = 0;
+            int lslot = 0;
             uint32_t chunk_phase = 0;
             bool ok = true;
             for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
                 for (int kb = 0; kb < p.num_kb; ++kb) {
+                    const int ls = lo_ring ? lslot : stage;
                     const bool chunk_start = (kb % p.chunk_kb) == 0;
                     const bool chunk_end = (kb % p.chunk_kb) == p.chunk_kb - 1 || kb == p.num_kb - 1;
                     if (chunk_start) {
@@ -506,8 +626,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t da = smem_desc(a_raw(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t db = smem_desc(b_raw(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                         if (split) {
-                            const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
-                            const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
+                            const uint64_t dal = smem_desc(a_lo(ls) + ks * a_kstep, a_lbo, a_sbo, a_lay);
+                            const uint64_t dbl = smem_desc(b_lo(ls) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                             mma(dal, db, accum);   // lo * hi
                             mma(da, dbl, 1u);      // hi * lo
                             mma(da, db, 1u);       // hi * hi
@@ -516,6 +636,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     commit_all(smem_u32(&ss->empty[stage]));   // frees the stage in every CTA
+                    if (lo_ring) {
+                        commit_all(smem_u32(&ss->lo_empty[ls]));   // and the lo slot
+                        if (++lslot == p.lo_slots) lslot = 0;
+                    }
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
                     if (chunk_end) {
                         commit_all(smem_u32(&ss->part_full));  // partial ready for promotion
@@ -529,41 +653,113 @@ __global__ void __launch_bounds__(kThreads, 1)
             drain_phase(smem_u32(&ss->drain), 0);
         }
         __syncwarp();
+    } else if (warp >= kExportWarp0) {
+        // ------------------------------------------------ export (fused all-gather)
+        // Follows the epilogue tile by tile: tile j of this CTA may be copied
+        // once all eight epilogue warps have counted it into tiles_stored.
+        if (p.export_peers && p.npeers > 0) {
+            const int et = threadIdx.x - kExportWarp0 * 32;
+            unsigned int j = 0;
+            for (int t = unit0; t < p.total_tiles; t += unit_step, ++j) {
+                if (!wait_count(&ss->tiles_stored, (unsigned int)kEpiWarps * (j + 1u), ss, p, kWaitExportTile))
+                    break;
+                __threadfence();
+                const TileCoord tc = decode_tile(t, p);
+                int idx[kMaxBatchDims];
+                batch_index(tc.batch, p, idx);
+                int64_t coff = 0;
+#pragma unroll
+                for (int d = 0; d < kMaxBatchDims; ++d)
+                    if (d < p.nbd) coff += (int64_t)idx[d] * p.c_bs[d];
+                const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
+                const int n0 = tc.nt * BN;
+                const int rows = min(kBM, p.M - m0);
+                const int cols = min(BN, p.N - n0);
+                if (rows <= 0 || cols <= 0) continue;
+                const int64_t off = coff + (p.peer_row0 + m0) * p.ldc + n0;
+                if (p.export_vec) export_tile<true>(p, off, rows, cols, et);
+                else export_tile<false>(p, off, rows, cols, et);
+            }
+            // the peers' rows have landed before the kernel is seen as complete
+            __threadfence_system();
+        }
     } else if (warp >= kSplitWarp0) {
         // ------------------------------------------------ split / stage relay
-        // Every thread waits for the stage itself and reports it itself: a
-        // warp-wide wait / arrive is one warp instruction, and no thread is held
-        // back by another's wake-up.
+        // Every thread waits for the stage itself; it reports the stage itself
+        // (a warp-wide wait / arrive is one warp instruction, and no thread is
+        // held back by another's wake-up), or with p.elect lane 0 reports the
+        // whole warp in one arrival of count 32.
         const int tid = threadIdx.x - kSplitWarp0 * 32;
         const bool compute_lo = p.split && !p.presplit;
+        const bool lo_ring = compute_lo && !p.lo_tied;
         int stage = 0;
         uint32_t phase = 0;
+        int lslot = 0;
+        uint32_t lphase = 0;
         bool ok = true;
         for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                const bool landed = p.relay_spin
+                bool landed = p.relay_spin
                     ? wait_phase<0>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)
                     : wait_phase<1>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull);
-                if (!landed) {
+                // lo ring: the MMAs that read this lo slot last time are done
+                if (landed && lo_ring)
+                    landed = wait_phase<1>(smem_u32(&ss->lo_empty[lslot]), lphase ^ 1u, ss, p, kWaitSplitFull);
+                // (per-warp reporting needs the whole warp to go on or stop together)
+                if (p.elect ? !__all_sync(0xffffffffu, landed) : !landed) {
                     ok = false;
                     break;
                 }
                 if (compute_lo) {
                     // The MMA reads the raw tile as hi (the TF32 datapath drops the
                     // 13 low mantissa bits); lo = x - hi is exact.
+                    const int ls = lo_ring ? lslot : stage;
                     const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes);
-                    uint4* lo = reinterpret_cast<uint4*>(smem + (size_t)stage * L::kStageBytes + raw_region);
+                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)ls * L::kStageBytes);
                     constexpr int n4 = (int)(L::kStageBytes / 16);
-#pragma unroll 4
-                    for (int i = tid; i < n4; i += kSplitThreads) {
-                        const uint4 x = raw[i];
-                        lo[i] = make_uint4(split_lo(x.x), split_lo(x.y), split_lo(x.z), split_lo(x.w));
+                    static_assert(n4 % kSplitThreads == 0, "stage not a whole number of split rounds");
+                    // all of this thread's loads first (they queue behind the
+                    // tensor core's reads of shared memory), then the stores
+                    constexpr int kPer = n4 / kSplitThreads;
+                    constexpr int kBatch = batch_of(kPer);
+                    static_assert(kPer % kBatch == 0, "split batches must tile the stage");
+#pragma unroll 1
+                    for (int i0 = 0; i0 < kPer; i0 += kBatch) {
+                        uint4 x[kBatch];
+#pragma unroll
+                        for (int u = 0; u < kBatch; ++u) x[u] = raw[tid + (i0 + u) * kSplitThreads];
+#pragma unroll
+                        for (int u = 0; u < kBatch; ++u)
+                            lo[tid + (i0 + u) * kSplitThreads] =
+                                make_uint4(split_lo(x[u].x), split_lo(x[u].y), split_lo(x[u].z), split_lo(x[u].w));
                     }
                     fence_proxy_async_smem();
+                    if (lo_ring && ++lslot == p.lo_slots) { lslot = 0; lphase ^= 1u; }
                 }
                 // stage ready (in this CTA) for the MMA issuer
-                if (kPair) mbar_arrive_cluster(split_done0 + (uint32_t)stage * 8u);
-                else mbar_arrive(smem_u32(&ss->split_done[stage]));
+                if (p.elect == 2) {
+                    // the last of the four split warps through this stage
+                    // reports all of them with one arrival
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence_block();
+                        const unsigned int before = atomicInc(&ss->split_warps_done[stage], kSplitThreads / 32 - 1);
+                        __threadfence_block();
+                        if (before == kSplitThreads / 32 - 1) {
+                            if (kPair) mbar_arrive_cluster_cnt(split_done0 + (uint32_t)stage * 8u, kSplitThreads);
+                            else mbar_arrive_cnt(smem_u32(&ss->split_done[stage]), kSplitThreads);
+                        }
+                    }
+                } else if (p.elect) {
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (kPair) mbar_arrive_cluster_cnt(split_done0 + (uint32_t)stage * 8u, 32u);
+                        else mbar_arrive_cnt(smem_u32(&ss->split_done[stage]), 32u);
+                    }
+                } else {
+                    if (kPair) mbar_arrive_cluster(split_done0 + (uint32_t)stage * 8u);
+                    else mbar_arrive(smem_u32(&ss->split_done[stage]));
+                }
                 if (++stage == stages) { stage = 0; phase ^= 1u; }
             }
         }
@@ -571,11 +767,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------ epilogue (warps 0-7)
         const int sub = warp & 3;                    // TMEM sub-partition = row group
         const int half = warp >> 2;                  // column half
-        constexpr int kHalf = BN / 2;
+        // column half h owns 32-column chunks [c_lo, c_hi) (BN / 32 may be odd)
+        const int c_lo = half * L::kHalfChunks;
+        const int c_hi = half ? L::kChunks : L::kHalfChunks;
         const int row = sub * 32 + lane;
         const uint32_t lane_base = tmem_base + ((uint32_t)(sub * 32) << 16);
-        const uint32_t t_part = lane_base + (uint32_t)(half * kHalf);
-        const uint32_t t_master = lane_base + (uint32_t)(BN + half * kHalf);
+        const uint32_t t_part = lane_base;
+        const uint32_t t_master = lane_base + (uint32_t)BN;
         float* stage_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes) +
                          warp * kStageFloatsPerWarp;                  // this warp's store staging block
         const bool has_bias = (p.epi & kEpiBias) != 0;
@@ -601,22 +799,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll 1
-                for (int j = 0; j < kHalf; j += 32) {
+                // the MMAs wait for this hand-off at every chunk, so it is kept
+                // short: both loads behind one wait, master stores not waited
+                // for until the partial has been released
+                for (int j = 32 * c_lo; j < 32 * c_hi; j += 32) {
                     uint32_t r[32];
-                    tmem_ld32(t_part + j, r);
                     if (c > 0) {
                         uint32_t m[32];
-                        tmem_ld32(t_master + j, m);
+                        tmem_ld32x2(t_part + j, r, t_master + j, m);
 #pragma unroll
                         for (int i = 0; i < 32; ++i)
                             r[i] = __float_as_uint(__uint_as_float(m[i]) + __uint_as_float(r[i]));
+                    } else {
+                        tmem_ld32(t_part + j, r);
                     }
-                    tmem_st32(t_master + j, r);
+                    tmem_st32_async(t_master + j, r);
                 }
                 tc_fence_before();
                 // the MMA may overwrite the partial once every epilogue thread has it
                 if (kPair) mbar_arrive_cluster(part_free0);
                 else mbar_arrive(smem_u32(&ss->part_free));
+                tmem_wait_st();   // the master is complete before this thread reads it again
                 chunk_phase ^= 1u;
             }
             if (!ok) break;
@@ -644,7 +847,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = tc.nt * BN;
             const int gm = m0 + row;
             const bool rok = gm < p.M;
-            float* crow = p.C + coff + (int64_t)(rok ? gm : 0) * p.ldc;
+            // export mode: this GPU's full C, at this rank's row offset
+            const int64_t crow_idx = rok ? gm + (p.export_peers ? p.peer_row0 : 0) : 0;
+            float* crow = p.C + coff + crow_idx * p.ldc;
             const float* brow = has_bias ? p.bias + boff + (int64_t)(rok ? gm : 0) * p.bias_rs : nullptr;
             const uint32_t t_row = lane_base + (uint32_t)BN;   // master, column 0
 
@@ -701,7 +906,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_arrive(smem_u32(&ss->master_free));
                 }
             } else {
-                for (int c = half * kHalf; c < (half + 1) * kHalf; c += 32) {
+                for (int c = 32 * c_lo; c < 32 * c_hi; c += 32) {
                     const int gn0 = n0 + c;
                     if (gn0 >= p.N) break;   // uniform across the warp
                     uint32_t r[32];
@@ -724,10 +929,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
+            if (p.export_peers) {
+                // this warp's part of the tile is in C (visible GPU-wide) for the export warps
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(&ss->tiles_stored, 1u);
+            }
         }
         // remote rows (fused all-gather) have landed and are visible
         // system-wide before the kernel is seen as complete
-        if (p.npeers > 0) {
+        if (p.npeers > 0 && !p.export_peers) {
             if (lane == 0) bulk_wait_all();
             __syncwarp();
             __threadfence_system();

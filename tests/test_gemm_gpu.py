@@ -171,13 +171,18 @@ def test_batched_broadcast_layouts(sa, sb, ta, tb, mode):
     assert_close(gpu_matmul(A, B, ta, tb), ob.oracle_matmul(A, B, ta, tb), mode, f"{sa}x{sb}")
 
 
-@pytest.fixture(params=["0", "1"], ids=["single_sm", "sm_pair"])
+@pytest.fixture(params=[("0", None), ("1", "256"), ("1", "224")],
+                ids=["single_sm", "sm_pair_256", "sm_pair_224"])
 def kernel_variant(request, monkeypatch):
     """Forces the single-SM (M=128 tiles) or the SM-pair (M=256 tiles,
-    cta_group::2) kernel through MG_GEMM_PAIR, which the library reads on
-    every call."""
-    monkeypatch.setenv("MG_GEMM_PAIR", request.param)
-    return request.param
+    cta_group::2) kernel through MG_GEMM_PAIR, and for pairs the tile width
+    (256, or 224 -- 112 B columns per SM, a partly filled last MN-major box)
+    through MG_GEMM_BN; the library reads both on every call."""
+    pair, bn = request.param
+    monkeypatch.setenv("MG_GEMM_PAIR", pair)
+    if bn is not None:
+        monkeypatch.setenv("MG_GEMM_BN", bn)
+    return f"pair={pair} bn={bn}"
 
 
 @pytest.mark.parametrize("mode", MODES)

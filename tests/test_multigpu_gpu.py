@@ -1,7 +1,10 @@
 """Row-sharded GEMM on 2 GPUs (one process each, NCCL): the all-gather fused
-into the GEMM epilogue (peer stores over NVLink) and the NCCL all-gather both
-leave the full C on every GPU, matching the oracle on sampled rows of each
-rank's block. Skipped when fewer than 2 GPUs are visible."""
+into the GEMM kernel and the NCCL all-gather both leave the full C on every
+GPU, matching the oracle on sampled rows of each rank's block. The fused path
+runs in both of its forms: export warps copying finished tiles to the peer
+(default) and the epilogue storing to every rank itself (MG_GEMM_EXPORT=0);
+a 1001-wide C takes the 4-byte copy paths. Skipped when fewer than 2 GPUs are
+visible."""
 import os
 import socket
 
@@ -46,8 +49,9 @@ def _worker(rank, world, port, n, q):
         A_local = torch.from_numpy(A[r0:r1].copy()).to(dev)
         Bg = torch.from_numpy(B).to(dev)
         report = {}
-        for mode in (_lib.MG_MODE_TF32X3, _lib.MG_MODE_TF32):
+        for mode, export in ((_lib.MG_MODE_TF32X3, "1"), (_lib.MG_MODE_TF32, "1"), (_lib.MG_MODE_TF32X3, "0")):
             lib.mg_set_mode(mode)
+            os.environ["MG_GEMM_EXPORT"] = export
             full = torch.full((n, n), float("nan"), device=dev)
             peers = PeerRows(full)
             for _ in range(2):                       # two calls in a row into the same buffers
@@ -62,7 +66,7 @@ def _worker(rank, world, port, n, q):
             rows = [0, 5, n // 2 - 1, n // 2, n // 2 + 7, n - 1]
             ref = ob.oracle_matmul(A[rows], B)
             tol = 1e-5 if mode == _lib.MG_MODE_TF32X3 else 2e-3
-            report[mode] = (bool(np.all(np.isfinite(got))), ob.frob_rel_err(got[rows], ref) <= tol,
+            report[(mode, export)] = (bool(np.all(np.isfinite(got))), ob.frob_rel_err(got[rows], ref) <= tol,
                             bool(np.array_equal(got, full_nccl.cpu().numpy())))
             dist.barrier()
             peers.close()
@@ -74,7 +78,8 @@ def _worker(rank, world, port, n, q):
             dist.destroy_process_group()
 
 
-def test_fused_all_gather_on_two_gpus():
+@pytest.mark.parametrize("n", [1024, 1001])
+def test_fused_all_gather_on_two_gpus(n):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -82,7 +87,7 @@ def test_fused_all_gather_on_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, 1024, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, n, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(2))
@@ -90,7 +95,8 @@ def test_fused_all_gather_on_two_gpus():
         p.join(timeout=60)
     for rank, rep in results.items():
         assert isinstance(rep, dict), f"rank {rank}: {rep}"
-        for mode, (finite, close, same) in rep.items():
-            assert finite, f"rank {rank} mode {mode}: C has rows nobody wrote"
-            assert close, f"rank {rank} mode {mode}: rows differ from the oracle"
-            assert same, f"rank {rank} mode {mode}: fused and NCCL all-gather differ"
+        for (mode, export), (finite, close, same) in rep.items():
+            what = f"rank {rank} mode {mode} export {export}"
+            assert finite, f"{what}: C has rows nobody wrote"
+            assert close, f"{what}: rows differ from the oracle"
+            assert same, f"{what}: fused and NCCL all-gather differ"
