@@ -34,9 +34,10 @@ METRIC = "fp32-accurate matmul TFLOP/s & % TF32 roofline at 1/2/4/8 B200 vs host
 UNIT = "TFLOP/s"
 WORKLOAD = "square fp32 GEMM 8192x8192x8192, rows of A sharded over the GPUs, C rows all-gathered"
 
-# DRAM bytes (read + write) of one launch of the GEMM kernel from the ncu
-# capture summarised in profiles/ (null until that capture exists).
-NCU_TRAFFIC_BYTES_PER_LAUNCH = {"3xtf32": None, "tf32": None}
+# DRAM bytes (read + write) of one 8192^3 launch of the GEMM kernel, from the
+# ncu capture summarised in profiles/dram_mg_gemm_tc_kernel_8192.md
+# (dram__bytes_read.sum + dram__bytes_write.sum; null where not captured).
+NCU_TRAFFIC_BYTES_PER_LAUNCH = {"3xtf32": 2568310272 + 255417856, "tf32": None}
 
 
 def parse_args():
@@ -49,6 +50,9 @@ def parse_args():
     p.add_argument("--size", type=int, default=SIZE)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", choices=["gemm", "decoder"], default="gemm",
+                   help="gemm: the square 8192^3 GEMM (default); decoder: the decoder-only character "
+                        "model's training step through the drop-in build, batch-sharded over the GPUs")
     p.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                    help="N>1: C rows reach every GPU from the GEMM epilogue over NVLink (fused) "
                         "or by an NCCL all-gather after it")
@@ -188,6 +192,8 @@ class ClockSampler:
 # ------------------------------------------------------------------ GPU side
 def main():
     args = parse_args()
+    if args.workload == "decoder":
+        return run_decoder(args)
     if args.impl == "reference":
         return run_reference_arm(args)
 
@@ -376,6 +382,145 @@ def main():
                       "note": "max over ranks of the per-rank GEMM time; the step adds the exchange "
                               "(the fence of the fused all-gather, or the NCCL all-gather)"},
         "exchange_ms": gather_ms if world > 1 else 0.0,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ decoder step
+DECODER_METRIC = "decoder training step tokens/s (6 layers, d_model 384, batch 64 x 256 tokens)"
+
+
+def run_decoder(args):
+    """The decoder-only character model's training step (6 layers, 6 heads,
+    d_model 384, MLP 1536, context 256, vocab 65, batch 64), built from the
+    reference's own modules through the drop-in build: forward, cross-entropy,
+    backward (every GEMM on the sm_100a kernels), gradient all-reduce over the
+    ranks (NCCL), AdamW step. The 64 sequences are split over the ranks (the
+    global batch stays 64: "strong" scaling). Reports
+    tokens/s, the step time, and the GEMMs' share of it (CUDA events around
+    every GEMM on the library stream, one extra observed step)."""
+    rank, local_rank, world = env_rank()
+    sys.path.insert(0, ROOT)
+    from macrograd_b200 import training
+
+    cfg = training.CONFIG
+    T = cfg["context"]
+    tokens_per_step = training.BATCH * T
+    if args.impl == "reference":
+        # the reference's own CPU step on one of its sequences (it is single-threaded)
+        if rank != 0:
+            return 0
+        m = training.DecoderStep(device="cpu")
+        m.make_batch(5, training.BATCH, T, 0, 1)
+        vals = []
+        for i in range(max(1, args.warmup) + max(1, args.steps)):
+            t0 = time.perf_counter()
+            m.forward_backward()
+            m.optimizer_step()
+            dt = time.perf_counter() - t0
+            if i >= max(1, args.warmup):
+                vals.append(T / dt)
+        m.close()
+        v = statistics.median(vals)
+        sample = f"1 sequence of {T} tokens per step (full model, forward + backward + AdamW), 1 core"
+        print(json.dumps({"impl": "reference", "metric": DECODER_METRIC, "value": v, "unit": "tokens/s",
+                          "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic token ids (reference CPU RNG)",
+                          "config": {"workload": "decoder training step", **cfg, "batch": training.BATCH},
+                          "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
+                                           "sample": sample},
+                          "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return 0
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    import macrograd_b200 as mg
+    from macrograd_b200 import _lib
+
+    lib = mg.load()
+    _lib.check(lib.mg_set_mode(_lib.MG_MODE_TF32X3 if args.mode == "3xtf32" else _lib.MG_MODE_TF32))
+    m = training.DecoderStep(device="cuda", device_index=local_rank)
+    first, count = training.shard(training.BATCH, world, rank)
+    m.make_batch(5, training.BATCH, T, first, count)
+    flat = torch.empty(m.numel, dtype=torch.float32, device=dev)
+
+    def step():
+        loss = m.forward_backward()
+        if world > 1:
+            m.allreduce_grads(flat=flat)
+        m.optimizer_step()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    # GEMM share: one observed step
+    m.observe(1)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    step()
+    m.lib.c5_synchronize()
+    t1.record()
+    torch.cuda.synchronize()
+    obs_step_ms = t0.elapsed_time(t1)
+    gemm_ms, gemm_flop, calls = m.gemm_ms(), m.gemm_flop(), m.gemm_calls()
+    m.observe(0)
+    launches0 = lib.mg_launch_count()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    torch.cuda.synchronize()
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    losses = []
+    for _ in range(args.steps):
+        losses.append(step())
+    m.lib.c5_synchronize()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    launches = lib.mg_launch_count() - launches0
+    t = torch.tensor([ev0.elapsed_time(ev1) / args.steps, gemm_ms, obs_step_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step, gemm_ms, obs_step_ms = float(t[0]), float(t[1]), float(t[2])
+    m.close()
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    value = tokens_per_step / (ms_per_step * 1e-3)
+    line = {
+        "metric": DECODER_METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic token ids (reference CPU RNG), random init",
+        "config": {"workload": "decoder training step (reference modules through the drop-in build)", **cfg,
+                   "batch": training.BATCH, "mode": args.mode,
+                   "parallelism": f"data-parallel x{world}" + (" + NCCL gradient all-reduce" if world > 1 else "")},
+        "gemm": {"calls_per_step": calls, "ms_per_step": gemm_ms, "share_of_step": gemm_ms / obs_step_ms,
+                 "tflops": gemm_flop / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None,
+                 "gflop_per_step_per_rank": gemm_flop / 1e9,
+                 "note": "CUDA events around every GEMM on the library stream, one observed step (max over ranks)"},
+        "loss": losses[-1] if losses else None,
+        "gpu_launches": int(launches),
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)

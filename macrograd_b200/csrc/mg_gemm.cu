@@ -429,26 +429,12 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     const int split = gp.split;
     // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
     const size_t fixed = 1024 + mg::kSharedStateBytes + (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4 + 64;
-    const size_t avail = (size_t)dev->max_smem - fixed;
-    const size_t sb = L::kStageBytes;
-    // 3xTF32: the lo tiles live in their own short ring (the split fills a slot
-    // just before its MMAs), so more shared memory goes to raw stages -- the
-    // TMA look-ahead. Pre-split lo planes arrive with their stage (tied).
-    int stages;
-    if (!split) {
-        stages = (int)(avail / sb);
-        gp.lo_slots = 0;
-    } else if (gp.lo_tied) {
-        stages = (int)(avail / (2 * sb));
-        gp.lo_slots = stages;
-    } else {
-        stages = (int)((avail - std::min(avail, (size_t)gp.lo_slots * sb)) / sb);
-    }
+    const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);   // raw (+ lo) tiles
+    int stages = (int)((size_t)(dev->max_smem - (int)fixed) / per_stage);
     stages = std::min(stages, mg::kMaxStages);
     if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
-    if (split && gp.lo_tied) gp.lo_slots = stages;
     gp.stages = stages;
-    const size_t smem = fixed + sb * (size_t)(stages + (split ? gp.lo_slots : 0));
+    const size_t smem = fixed + per_stage * stages;
     auto k = kernel_of<BN, kPair>();
     const int slot = bn_slot(BN) + (kPair ? 4 : 0);
     if (dev->attr_smem[slot] < smem) {
@@ -752,9 +738,6 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);
     gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
     gp.presplit = presplit ? 1 : 0;
-    gp.lo_tied = (presplit || !tuning_int("MG_GEMM_LO_RING", 0, 0, 1)) ? 1 : 0;
-    gp.lo_slots = tuning_int("MG_GEMM_LO_SLOTS", 2, 1, 4);
-    gp.elect = tuning_int("MG_GEMM_ELECT", 0, 0, 2);
     gp.a_mn = a_mn;
     gp.b_mn = b_mn;
     gp.a_rank = 2 + am.nmap;

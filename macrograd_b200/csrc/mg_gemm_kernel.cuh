@@ -108,9 +108,6 @@ struct GemmParams {
     int relay_spin;             // split warps poll without suspend hints
     int split;                  // 1 = 3xTF32
     int presplit;               // 3xTF32 with lo planes precomputed in HBM (tmAlo / tmBlo)
-    int lo_slots;               // 3xTF32: lo tiles in shared memory (a ring, or one per stage)
-    int lo_tied;                // 1: lo slot = stage (freed with it); 0: separate ring of lo_slots
-    int elect;                  // split warps report a stage: 0 per thread, 1 per warp, 2 per CTA
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
     int a_rank, b_rank;         // tensor-map ranks (2 + mapped batch dims)
     uint32_t idesc;
@@ -186,7 +183,6 @@ struct SharedState {
     uint64_t full[kMaxStages];        // local: TMA landed
     uint64_t split_done[kMaxStages];  // MMA issuer's CTA: stage ready in every CTA
     uint64_t empty[kMaxStages];       // local: the MMAs reading the stage are done
-    uint64_t lo_empty[kMaxStages];    // local: the MMAs reading the lo slot are done (lo ring)
     uint64_t part_full;               // local: partial accumulator complete
     uint64_t part_free;               // MMA issuer's CTA: every epilogue took the partial
     uint64_t master_done;             // local (softmax): every epilogue thread wrote its master half
@@ -195,7 +191,6 @@ struct SharedState {
     uint32_t tmem_base;
     volatile int abort_flag;
     unsigned int tiles_stored;        // epilogue warps x tiles written to C (export mode)
-    unsigned int split_warps_done[kMaxStages];   // elect == 2: split warps through the stage
 };
 
 static_assert(sizeof(SharedState) <= kSharedStateBytes, "SharedState outgrew its slot");
@@ -443,15 +438,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const uint32_t smem_base = smem_u32(smem);
     const int stages = p.stages;
-    // shared memory: raw stages, then (3xTF32) the lo slots, then the barriers
+    // shared memory: raw stages, then (3xTF32) one lo tile per stage, then the barriers
     const uint32_t raw_region = (uint32_t)stages * L::kStageBytes;
-    const uint32_t lo_region = p.split ? (uint32_t)p.lo_slots * L::kStageBytes : 0u;
-    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region + lo_region);
+    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region * (p.split ? 2u : 1u));
 
     auto a_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes; };
     auto b_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes + L::kABytes; };
-    auto a_lo = [&](int l) { return smem_base + raw_region + (uint32_t)l * L::kStageBytes; };
-    auto b_lo = [&](int l) { return a_lo(l) + L::kABytes; };
+    auto a_lo = [&](int s) { return a_raw(s) + raw_region; };
+    auto b_lo = [&](int s) { return b_raw(s) + raw_region; };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -466,10 +460,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&ss->full[s]), 1);
             mbar_init(smem_u32(&ss->split_done[s]), kSplitThreads * (kPair ? 2 : 1));
             mbar_init(smem_u32(&ss->empty[s]), 1);
-        }
-        for (int l = 0; l < kMaxStages; ++l) {
-            mbar_init(smem_u32(&ss->lo_empty[l]), 1);
-            ss->split_warps_done[l] = 0u;
         }
         mbar_init(smem_u32(&ss->part_full), 1);
         mbar_init(smem_u32(&ss->part_free), kEpiThreads * (kPair ? 2 : 1));
@@ -595,15 +585,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kPair) tc_commit_pair_all(bar, (uint16_t)0x3);
                 else tc_commit(bar);
             };
-            const bool lo_ring = split && !p.lo_tied;
             int stage = 0;
             uint32_t phase = 0;
-            int lslot = 0;
             uint32_t chunk_phase = 0;
             bool ok = true;
             for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    const int ls = lo_ring ? lslot : stage;
                     const bool chunk_start = (kb % p.chunk_kb) == 0;
                     const bool chunk_end = (kb % p.chunk_kb) == p.chunk_kb - 1 || kb == p.num_kb - 1;
                     if (chunk_start) {
@@ -626,8 +613,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint64_t da = smem_desc(a_raw(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t db = smem_desc(b_raw(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                         if (split) {
-                            const uint64_t dal = smem_desc(a_lo(ls) + ks * a_kstep, a_lbo, a_sbo, a_lay);
-                            const uint64_t dbl = smem_desc(b_lo(ls) + ks * b_kstep, b_lbo, b_sbo, b_lay);
+                            const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
+                            const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                             mma(dal, db, accum);   // lo * hi
                             mma(da, dbl, 1u);      // hi * lo
                             mma(da, db, 1u);       // hi * hi
@@ -636,10 +623,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     commit_all(smem_u32(&ss->empty[stage]));   // frees the stage in every CTA
-                    if (lo_ring) {
-                        commit_all(smem_u32(&ss->lo_empty[ls]));   // and the lo slot
-                        if (++lslot == p.lo_slots) lslot = 0;
-                    }
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
                     if (chunk_end) {
                         commit_all(smem_u32(&ss->part_full));  // partial ready for promotion
@@ -685,37 +668,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= kSplitWarp0) {
         // ------------------------------------------------ split / stage relay
-        // Every thread waits for the stage itself; it reports the stage itself
-        // (a warp-wide wait / arrive is one warp instruction, and no thread is
-        // held back by another's wake-up), or with p.elect lane 0 reports the
-        // whole warp in one arrival of count 32.
+        // Every thread waits for the stage itself and reports it itself: a
+        // warp-wide wait / arrive is one warp instruction, and no thread is held
+        // back by another's wake-up (one elected arrival per warp or per CTA
+        // measured slower).
         const int tid = threadIdx.x - kSplitWarp0 * 32;
         const bool compute_lo = p.split && !p.presplit;
-        const bool lo_ring = compute_lo && !p.lo_tied;
         int stage = 0;
         uint32_t phase = 0;
-        int lslot = 0;
-        uint32_t lphase = 0;
         bool ok = true;
         for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 bool landed = p.relay_spin
                     ? wait_phase<0>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)
                     : wait_phase<1>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull);
-                // lo ring: the MMAs that read this lo slot last time are done
-                if (landed && lo_ring)
-                    landed = wait_phase<1>(smem_u32(&ss->lo_empty[lslot]), lphase ^ 1u, ss, p, kWaitSplitFull);
-                // (per-warp reporting needs the whole warp to go on or stop together)
-                if (p.elect ? !__all_sync(0xffffffffu, landed) : !landed) {
+                if (!landed) {
                     ok = false;
                     break;
                 }
                 if (compute_lo) {
                     // The MMA reads the raw tile as hi (the TF32 datapath drops the
                     // 13 low mantissa bits); lo = x - hi is exact.
-                    const int ls = lo_ring ? lslot : stage;
                     const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes);
-                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)ls * L::kStageBytes);
+                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)stage * L::kStageBytes);
                     constexpr int n4 = (int)(L::kStageBytes / 16);
                     static_assert(n4 % kSplitThreads == 0, "stage not a whole number of split rounds");
                     // all of this thread's loads first (they queue behind the
@@ -734,32 +709,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 make_uint4(split_lo(x[u].x), split_lo(x[u].y), split_lo(x[u].z), split_lo(x[u].w));
                     }
                     fence_proxy_async_smem();
-                    if (lo_ring && ++lslot == p.lo_slots) { lslot = 0; lphase ^= 1u; }
                 }
                 // stage ready (in this CTA) for the MMA issuer
-                if (p.elect == 2) {
-                    // the last of the four split warps through this stage
-                    // reports all of them with one arrival
-                    __syncwarp();
-                    if (lane == 0) {
-                        __threadfence_block();
-                        const unsigned int before = atomicInc(&ss->split_warps_done[stage], kSplitThreads / 32 - 1);
-                        __threadfence_block();
-                        if (before == kSplitThreads / 32 - 1) {
-                            if (kPair) mbar_arrive_cluster_cnt(split_done0 + (uint32_t)stage * 8u, kSplitThreads);
-                            else mbar_arrive_cnt(smem_u32(&ss->split_done[stage]), kSplitThreads);
-                        }
-                    }
-                } else if (p.elect) {
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (kPair) mbar_arrive_cluster_cnt(split_done0 + (uint32_t)stage * 8u, 32u);
-                        else mbar_arrive_cnt(smem_u32(&ss->split_done[stage]), 32u);
-                    }
-                } else {
-                    if (kPair) mbar_arrive_cluster(split_done0 + (uint32_t)stage * 8u);
-                    else mbar_arrive(smem_u32(&ss->split_done[stage]));
-                }
+                if (kPair) mbar_arrive_cluster(split_done0 + (uint32_t)stage * 8u);
+                else mbar_arrive(smem_u32(&ss->split_done[stage]));
                 if (++stage == stages) { stage = 0; phase ^= 1u; }
             }
         }

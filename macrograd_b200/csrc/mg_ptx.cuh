@@ -43,12 +43,6 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// one arrival standing for `count` (e.g. a whole warp after __syncwarp)
-__device__ __forceinline__ void mbar_arrive_cnt(uint32_t bar, uint32_t count)
-{
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
 // true once the phase with the given parity has completed
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity)
 {
@@ -168,12 +162,6 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t addr, uint32_t rank)
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
 {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster_cnt(uint32_t cluster_addr, uint32_t count)
-{
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_addr), "r"(count)
-                 : "memory");
 }
 
 // try_wait with acquire at cluster scope: pairs with mbar_arrive_cluster from
