@@ -338,7 +338,7 @@ __global__ void k0_fill_kernel(FillParams p)
 // pieces of that fixed buffer instead and never allocates or frees.
 struct Workspace {
     void* stream;
-    void* ptrs[4] = {nullptr, nullptr, nullptr, nullptr};
+    void* ptrs[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     int n = 0;
     uint8_t* arena = nullptr;
     size_t arena_cap = 0, arena_used = 0;
@@ -421,9 +421,93 @@ mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace&
     return MG_OK;
 }
 
+int tuning_int(const char* name, int dflt, int lo, int hi);
+
+// Plans the split of the last, partial wave of tiles over the K dimension
+// (GemmParams::nlev): with `units` CTAs (pairs) resident, whole tiles fill
+// floor(T / units) waves; the R remaining tiles are cut into K-ranges so that
+// every unit gets work -- all R tiles at once in floor(units / R) ranges each
+// when that is >= 2, else level by level, 2, 4, 8... ranges per tile, as many
+// tiles per level as the units allow. Besides filling the idle units, the
+// levels finish their tiles at staggered times (the fused all-gather then
+// sends them while the later levels compute). Returns the workspace slots
+// needed (0: no split, every unit a whole tile).
+int plan_split(mg::GemmParams& gp, int units)
+{
+    gp.full_tiles = gp.total_tiles;
+    gp.nlev = 0;
+    if (units < 2 || !tuning_int("MG_GEMM_SPLIT", 1, 0, 1)) return 0;
+    const int T = gp.total_tiles, KB = gp.num_kb;
+    const int waves = T / units, R = T - waves * units;
+    if (R == 0) return 0;
+    const int min_kb = tuning_int("MG_GEMM_SPLIT_MIN_KB", 16, 1, 1 << 20);   // K-blocks per range at least
+    int S[mg::kMaxLevels], Rl[mg::kMaxLevels], n = 0, rem = R;
+    double t = 0.0;
+    if (units / R >= 2) {
+        const int s = std::min(std::min(units / R, 8), KB / min_kb);
+        if (s >= 2) {
+            S[0] = s;
+            Rl[0] = R;
+            n = 1;
+            rem = 0;
+            t = 1.0 / s;
+        }
+    } else {
+        for (int s = 2; rem > 0 && n < mg::kMaxLevels && KB / s >= min_kb; s *= 2) {
+            const int r = std::min(rem, units / s);
+            if (r == 0) break;
+            S[n] = s;
+            Rl[n] = r;
+            ++n;
+            rem -= r;
+            t += 1.0 / s;
+        }
+    }
+    if (rem > 0 || n == 0) return 0;
+    if (waves + t > 0.95 * (waves + 1)) return 0;   // not worth the partial sums
+    gp.full_tiles = waves * units;
+    int tile0 = gp.full_tiles, slot0 = 0;
+    for (int l = 0; l < n; ++l) {
+        gp.lev_split[l] = S[l];
+        gp.lev_tiles[l] = Rl[l];
+        gp.lev_tile0[l] = tile0;
+        gp.lev_slot0[l] = slot0;
+        tile0 += Rl[l];
+        slot0 += Rl[l] * (S[l] - 1);
+    }
+    gp.nlev = n;
+    return slot0;
+}
+
+// Plans the K split for `units` resident CTAs (pairs) and takes its workspace:
+// one slot of 2 x 128 x BN floats per partial range (both CTAs of a pair) plus
+// a zeroed counter per slot and CTA. Without workspace the launch goes unsplit.
+template <int BN>
+bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, bool allow)
+{
+    const int nslots = allow ? plan_split(gp, units) : 0;
+    if (nslots == 0) {
+        gp.full_tiles = gp.total_tiles;
+        gp.nlev = 0;
+        return false;
+    }
+    const size_t part = (size_t)nslots * 2 * mg::kBM * BN * sizeof(float);
+    const size_t flags = (size_t)nslots * 2 * sizeof(unsigned int);
+    uint8_t* w = static_cast<uint8_t*>(ws ? ws->get(part + flags) : nullptr);
+    if (!w || cudaMemsetAsync(w + part, 0, flags, st) != cudaSuccess) {
+        gp.full_tiles = gp.total_tiles;
+        gp.nlev = 0;
+        return false;
+    }
+    gp.part_ws = reinterpret_cast<float*>(w);
+    gp.part_flag = reinterpret_cast<unsigned int*>(w + part);
+    return true;
+}
+
 template <int BN, bool kPair>
 mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& malo,
-                    const CUtensorMap& mblo, mg::GemmParams& gp, const mg::PeerMaps& pm, cudaStream_t st)
+                    const CUtensorMap& mblo, mg::GemmParams& gp, const mg::PeerMaps& pm, cudaStream_t st,
+                    Workspace* ws, bool allow_split)
 {
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
@@ -461,10 +545,49 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             MG_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, k, &cfg));
             dev->max_clusters[slot - 4] = std::max(1, std::min(n, dev->sm_count / 2));
         }
-        const int pairs = std::max(1, std::min(gp.total_tiles, dev->max_clusters[slot - 4]));
+        const int resident = dev->max_clusters[slot - 4];
+        if (setup_split<BN>(gp, resident, ws, st, allow_split)) {
+            // the final K-ranges wait for partials from other CTAs of the grid:
+            // launch it cooperatively, so every CTA is resident at once
+            cudaLaunchAttribute attr2[2] = {attr[0], {}};
+            attr2[1].id = cudaLaunchAttributeCooperative;
+            attr2[1].val.cooperative = 1;
+            cfg.attrs = attr2;
+            cfg.numAttrs = 2;
+            cfg.gridDim = dim3((unsigned)(2 * resident), 1, 1);
+            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm) == cudaSuccess) {
+                g_launches++;
+                return MG_OK;
+            }
+            (void)cudaGetLastError();   // not launchable cooperatively here: run unsplit
+            gp.full_tiles = gp.total_tiles;
+            gp.nlev = 0;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+        }
+        const int pairs = std::max(1, std::min(gp.total_tiles, resident));
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
         MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm));
     } else {
+        if (setup_split<BN>(gp, dev->sm_count, ws, st, allow_split)) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)dev->sm_count, 1, 1);
+            cfg.blockDim = dim3(mg::kThreads, 1, 1);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeCooperative;
+            attr[0].val.cooperative = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm) == cudaSuccess) {
+                g_launches++;
+                return MG_OK;
+            }
+            (void)cudaGetLastError();
+            gp.full_tiles = gp.total_tiles;
+            gp.nlev = 0;
+        }
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
         k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, gp, pm);
         MG_CUDA_TRY(cudaGetLastError());
@@ -733,6 +856,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const int64_t total = nbatch * gp.tiles_per_batch;
     if (total >= (1ll << 31)) return fail(MG_ERR_UNSUPPORTED, "too many output tiles (%lld)", (long long)total);
     gp.total_tiles = (int)total;
+    gp.full_tiles = gp.total_tiles;   // no K split unless launch_tc plans one
     gp.group_m = 16;
     gp.chunk_kb = tuning_int("MG_GEMM_CHUNK_KB", mg::kChunkKb, 1, 64);
     gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);
@@ -809,18 +933,20 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
         }
     }
 
+    // the row softmax needs whole rows in one tile: no K split there
+    const bool allow_split = (d->epilogue & MG_EPI_SOFTMAX) == 0;
     if (pair) {
         switch (bn) {
-        case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, pm, st);
-        case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, pm, st);
-        case 224: return launch_tc<224, true>(dev, ma, mb, malo, mblo, gp, pm, st);
-        default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, pm, st);
+        case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+        case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+        case 224: return launch_tc<224, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+        default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
         }
     }
     switch (bn) {
-    case 64: return launch_tc<64, false>(dev, ma, mb, malo, mblo, gp, pm, st);
-    case 128: return launch_tc<128, false>(dev, ma, mb, malo, mblo, gp, pm, st);
-    default: return launch_tc<256, false>(dev, ma, mb, malo, mblo, gp, pm, st);
+    case 64: return launch_tc<64, false>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+    case 128: return launch_tc<128, false>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+    default: return launch_tc<256, false>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
     }
 }
 

@@ -78,6 +78,7 @@ constexpr int kExportThreads = 64;
 constexpr int kThreads = 16 * 32;
 constexpr int kMaxBatchDims = 6;
 constexpr int kMaxPeers = 8;
+constexpr int kMaxLevels = 4;       // split levels of the last partial wave
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
 constexpr uint32_t kSleepHintNs = 20000u;          // try_wait suspend hint
@@ -93,7 +94,8 @@ enum : int {
     kWaitEpiloguePartial = 5,
     kWaitEpilogueMaster = 6,
     kWaitEpilogueMasterFree = 7,
-    kWaitExportTile = 8
+    kWaitExportTile = 8,
+    kWaitPartials = 9
 };
 
 struct GemmParams {
@@ -136,6 +138,18 @@ struct GemmParams {
     int export_peers;
     int export_vec;             // N, ldc and every destination allow 16-byte copies
     float* peers[kMaxPeers];
+    // Work units. Whole tiles [0, full_tiles) are dealt round-robin to the
+    // CTAs (pairs). The rest -- the last, partial wave -- is split over the
+    // K dimension in up to kMaxLevels levels: level l takes lev_tiles[l] tiles
+    // from lev_tile0[l], cuts each into lev_split[l] K-ranges and gives one
+    // range to each of CTAs (pairs) 0 .. lev_tiles[l] * lev_split[l] - 1. The
+    // last range of a tile adds the other ranges' fp32 partials (workspace
+    // slots from lev_slot0[l]) into its output, in range order.
+    int full_tiles;
+    int nlev;
+    int lev_split[kMaxLevels], lev_tiles[kMaxLevels], lev_tile0[kMaxLevels], lev_slot0[kMaxLevels];
+    float* part_ws;             // [slot][cta rank][BN/32 chunks][128 rows][32] floats
+    unsigned int* part_flag;    // [slot][cta rank]: epilogue warps that stored their part
 };
 
 // 2-D tensor maps over every rank's full C (fused all-gather with TMA stores).
@@ -146,6 +160,45 @@ struct PeerMaps {
 struct TileCoord {
     int batch, mt, nt;
 };
+
+// One work unit: K-blocks [kb0, kb1) of a tile; kind 0 = the whole tile,
+// 1 = a partial range (stores its fp32 sum in workspace slot `slot`),
+// 2 = the final range (adds slots slot .. slot + nsib - 1 and writes C).
+struct Unit {
+    int tile, kb0, kb1, kind, slot, nsib;
+};
+
+// The i-th unit of CTA (pair) u0 of ustep; false past the last one. Every role
+// of the CTA walks the same list.
+__device__ __forceinline__ bool unit_at(const GemmParams& p, int u0, int ustep, int i, Unit& u)
+{
+    const int nw = p.full_tiles > u0 ? (p.full_tiles - u0 + ustep - 1) / ustep : 0;
+    if (i < nw) {
+        u.tile = u0 + i * ustep;
+        u.kb0 = 0;
+        u.kb1 = p.num_kb;
+        u.kind = 0;
+        u.slot = 0;
+        u.nsib = 0;
+        return true;
+    }
+    int j = i - nw;
+    for (int l = 0; l < p.nlev; ++l) {
+        const int S = p.lev_split[l];
+        if (u0 >= p.lev_tiles[l] * S) continue;
+        if (j-- > 0) continue;
+        const int tl = u0 / S, part = u0 - tl * S;
+        u.tile = p.lev_tile0[l] + tl;
+        u.kb0 = (int)((int64_t)p.num_kb * part / S);
+        u.kb1 = (int)((int64_t)p.num_kb * (part + 1) / S);
+        const int base = p.lev_slot0[l] + tl * (S - 1);
+        u.kind = part == S - 1 ? 2 : 1;
+        u.slot = part == S - 1 ? base : base + part;
+        u.nsib = part == S - 1 ? S - 1 : 0;
+        return true;
+    }
+    return false;
+}
 
 __device__ __forceinline__ TileCoord decode_tile(int t, const GemmParams& p)
 {
@@ -418,6 +471,69 @@ __device__ __forceinline__ void export_tile(const GemmParams& p, int64_t off, in
     }
 }
 
+// K-split partial sums. A slot holds one CTA's 128 x BN fp32 partial in the
+// epilogue threads' own layout: [32-column chunk][8 float4 columns][128 rows]
+// of float4, so one warp instruction moves 32 consecutive rows x 16 bytes --
+// 512 contiguous bytes -- and the final range's same thread reads back what
+// the partial range's same thread wrote. Kept out of line: they run once per
+// split unit and would otherwise crowd the epilogue main loop's registers.
+__device__ __noinline__ void store_partial(float* slot, uint32_t t_master, int c_lo, int c_hi, int row)
+{
+    float4* base = reinterpret_cast<float4*>(slot) + row;
+    for (int c = c_lo; c < c_hi; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_master + (uint32_t)(32 * c), r);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            base[(size_t)(c * 8 + q) * kBM] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                          __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+    }
+}
+
+// master += slots 0 .. nsib-1 (slot_stride floats apart), in slot order; two
+// slots' loads in flight at a time.
+__device__ __noinline__ void add_partials(const float* slot0, int nsib, size_t slot_stride, uint32_t t_master,
+                                          int c_lo, int c_hi, int row)
+{
+    const float4* base = reinterpret_cast<const float4*>(slot0) + row;
+    const size_t stride4 = slot_stride / 4;
+    for (int c = c_lo; c < c_hi; ++c) {
+        uint32_t r[32];
+        const uint32_t tcol = t_master + (uint32_t)(32 * c);
+        tmem_ld32(tcol, r);
+        auto add = [&](const float4& x, int e) {
+            r[4 * e] = __float_as_uint(__uint_as_float(r[4 * e]) + x.x);
+            r[4 * e + 1] = __float_as_uint(__uint_as_float(r[4 * e + 1]) + x.y);
+            r[4 * e + 2] = __float_as_uint(__uint_as_float(r[4 * e + 2]) + x.z);
+            r[4 * e + 3] = __float_as_uint(__uint_as_float(r[4 * e + 3]) + x.w);
+        };
+        int q = 0;
+        for (; q + 1 < nsib; q += 2) {
+            const float4* s0 = base + q * stride4 + (size_t)c * 8 * kBM;
+            const float4* s1 = s0 + stride4;
+            float4 x0[8], x1[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                x0[e] = __ldcg(s0 + (size_t)e * kBM);
+                x1[e] = __ldcg(s1 + (size_t)e * kBM);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) add(x0[e], e);   // slot q before slot q + 1
+#pragma unroll
+            for (int e = 0; e < 8; ++e) add(x1[e], e);
+        }
+        if (q < nsib) {
+            const float4* s0 = base + q * stride4 + (size_t)c * 8 * kBM;
+            float4 x0[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x0[e] = __ldcg(s0 + (size_t)e * kBM);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) add(x0[e], e);
+        }
+        tmem_st32(tcol, r);
+    }
+}
+
 // tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
 // tmBlo map their lo planes (same layout), which the producer loads next to
 // the raw tiles instead of the split warps computing them.
@@ -503,8 +619,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued = 0, issued_par = 0;
             bool ok = true;
-            for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
-                const TileCoord tc = decode_tile(t, p);
+            Unit u;
+            for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+                const TileCoord tc = decode_tile(u.tile, p);
                 int idx[kMaxBatchDims];
                 batch_index(tc.batch, p, idx);
                 int32_t a2 = 0, a3 = 0, a4 = 0, b2 = 0, b3 = 0, b4 = 0;
@@ -523,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
                 const int n0 = tc.nt * BN + (int)rank * L::kBRows;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!wait_phase<0>(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
                         ok = false;
                         break;
@@ -589,10 +706,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             uint32_t chunk_phase = 0;
             bool ok = true;
-            for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
-                for (int kb = 0; kb < p.num_kb; ++kb) {
-                    const bool chunk_start = (kb % p.chunk_kb) == 0;
-                    const bool chunk_end = (kb % p.chunk_kb) == p.chunk_kb - 1 || kb == p.num_kb - 1;
+            Unit u;
+            for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+                for (int kb = u.kb0; kb < u.kb1; ++kb) {
+                    const int rel = kb - u.kb0;   // chunks restart with every unit
+                    const bool chunk_start = (rel % p.chunk_kb) == 0;
+                    const bool chunk_end = (rel % p.chunk_kb) == p.chunk_kb - 1 || kb == u.kb1 - 1;
                     if (chunk_start) {
                         // every epilogue has taken the previous partial
                         if (!wait_phase<kPair ? 2 : 0>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
@@ -643,11 +762,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.export_peers && p.npeers > 0) {
             const int et = threadIdx.x - kExportWarp0 * 32;
             unsigned int j = 0;
-            for (int t = unit0; t < p.total_tiles; t += unit_step, ++j) {
+            Unit u;
+            for (int ui = 0; unit_at(p, unit0, unit_step, ui, u); ++ui, ++j) {
                 if (!wait_count(&ss->tiles_stored, (unsigned int)kEpiWarps * (j + 1u), ss, p, kWaitExportTile))
                     break;
+                if (u.kind == 1) continue;   // a partial K-range: its tile leaves with the final range
                 __threadfence();
-                const TileCoord tc = decode_tile(t, p);
+                const TileCoord tc = decode_tile(u.tile, p);
                 int idx[kMaxBatchDims];
                 batch_index(tc.batch, p, idx);
                 int64_t coff = 0;
@@ -677,8 +798,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         int stage = 0;
         uint32_t phase = 0;
         bool ok = true;
-        for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
-            for (int kb = 0; kb < p.num_kb; ++kb) {
+        Unit u;
+        for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+            for (int kb = u.kb0; kb < u.kb1; ++kb) {
                 bool landed = p.relay_spin
                     ? wait_phase<0>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull)
                     : wait_phase<1>(smem_u32(&ss->full[stage]), phase, ss, p, kWaitSplitFull);
@@ -735,9 +857,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t md_phase = 0;
         uint32_t mf_phase = 0;
         bool ok = true;
-        for (int t = unit0; ok && t < p.total_tiles; t += unit_step) {
-            const TileCoord tc = decode_tile(t, p);
-            const int n_chunks = (p.num_kb + p.chunk_kb - 1) / p.chunk_kb;
+        Unit u;
+        for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+            const TileCoord tc = decode_tile(u.tile, p);
+            const int n_chunks = (u.kb1 - u.kb0 + p.chunk_kb - 1) / p.chunk_kb;
             if (softmax && half == 1) {
                 // warps 0-3 read the whole master row of the previous tile; do
                 // not overwrite this half before they are done with it
@@ -783,6 +906,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 md_phase ^= 1u;
                 if (!__all_sync(0xffffffffu, synced)) break;
                 tc_fence_after();
+            }
+
+            if (u.kind == 1) {
+                // A partial K-range: the master goes to its workspace slot for
+                // the tile's final range to add; nothing is written to C.
+                store_partial(p.part_ws + (size_t)(u.slot * 2 + (int)rank) * (kBM * BN), lane_base + (uint32_t)BN,
+                              c_lo, c_hi, row);
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(&p.part_flag[u.slot * 2 + (int)rank], 1u);
+                tc_fence_before();
+                if (p.export_peers) {
+                    __syncwarp();
+                    if (lane == 0) atomicAdd(&ss->tiles_stored, 1u);
+                }
+                continue;
+            }
+            if (u.kind == 2) {
+                // the final range: every other range of the tile has stored its part
+                bool ready = true;
+                if (lane == 0)
+                    for (int q = 0; q < u.nsib && ready; ++q)
+                        ready = wait_count(&p.part_flag[(u.slot + q) * 2 + (int)rank], (unsigned int)kEpiWarps, ss, p,
+                                           kWaitPartials);
+                if (!__shfl_sync(0xffffffffu, ready ? 1 : 0, 0)) {
+                    ok = false;
+                    break;
+                }
+                __threadfence();
+                // master += the other ranges' partials, in range order
+                add_partials(p.part_ws + (size_t)(u.slot * 2 + (int)rank) * (kBM * BN), u.nsib,
+                             (size_t)2 * kBM * BN, lane_base + (uint32_t)BN, c_lo, c_hi, row);
             }
 
             // ---- output epilogue from the master

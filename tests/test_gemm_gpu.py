@@ -241,6 +241,48 @@ def test_kernel_variants_softmax_and_accumulate(kernel_variant):
     assert_close(host(g), prev + dW, 0, f"beta=1 {kernel_variant}")
 
 
+@pytest.mark.parametrize("pair", ["1", "0"], ids=["sm_pair", "single_sm"])
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("sa,sb,ta,tb,bias_shape", [
+    ((512, 1024), (1024, 1024), False, False, None),      # few tiles: one level, up to 8 K-ranges a tile
+    ((2048, 256), (256, 4096), False, False, None),       # 128 pair tiles: whole wave + 2- and 4-way levels
+    ((300, 1000), (700, 1000), False, True, (700,)),      # tails in M and N, bias added once
+    ((1000, 640), (1000, 520), True, False, (1, 520)),    # MN-major A
+])
+def test_k_split_of_the_last_wave(monkeypatch, pair, mode, sa, sb, ta, tb, bias_shape):
+    """The last, partial wave of tiles split over K (ranges summed in fp32 by
+    the final range of each tile); MG_GEMM_SPLIT_MIN_KB=1 lets short K split
+    too. Same tolerance as unsplit, and the unsplit launch agrees."""
+    monkeypatch.setenv("MG_GEMM_PAIR", pair)
+    monkeypatch.setenv("MG_GEMM_SPLIT_MIN_KB", "1")
+    set_mode(mode)
+    A = ob.seeded_uniform(sa, 841)
+    B = ob.seeded_uniform(sb, 842)
+    bias = ob.seeded_uniform(bias_shape, 843) if bias_shape else None
+    ref = ob.oracle_matmul(A, B, ta, tb, bias)
+    split = gpu_matmul(A, B, ta, tb, bias)
+    assert_close(split, ref, mode, "split")
+    monkeypatch.setenv("MG_GEMM_SPLIT", "0")
+    unsplit = gpu_matmul(A, B, ta, tb, bias)
+    assert_close(unsplit, ref, mode, "unsplit")
+    # the split launch really ran: its ranges are summed in another order
+    assert not np.array_equal(split, unsplit)
+
+
+def test_k_split_with_accumulate(monkeypatch):
+    """beta = 1 (gradient accumulation) is applied once, by the final range."""
+    monkeypatch.setenv("MG_GEMM_SPLIT_MIN_KB", "1")
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform((6, 400, 96), 851)
+    W = ob.seeded_uniform((96, 300), 852)
+    dC = ob.seeded_normal((6, 400, 300), 853)
+    prev = ob.seeded_normal((96, 300), 854)
+    g = cuda(prev)
+    F.matmul_backward(cuda(A), cuda(W), cuda(dC), need_a=False, grad_b=g)
+    _, dW, _ = ob.oracle_matmul_backward(A, W, dC)
+    assert_close(host(g), prev + dW, 0, "beta=1 split")
+
+
 @pytest.mark.parametrize("bias_shape", [(40,), (1, 40), (30, 1), (30, 40), (3, 1, 40), (3, 30, 40)])
 def test_bias_broadcast_forms(bias_shape):
     set_mode(_lib.MG_MODE_TF32X3)
