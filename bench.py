@@ -50,9 +50,12 @@ def parse_args():
     p.add_argument("--size", type=int, default=SIZE)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=["gemm", "decoder"], default="gemm",
+    p.add_argument("--workload", choices=["gemm", "decoder", "batched", "linear", "attention"], default="gemm",
                    help="gemm: the square 8192^3 GEMM (default); decoder: the decoder-only character "
-                        "model's training step through the drop-in build, batch-sharded over the GPUs")
+                        "model's training step through the drop-in build, batch-sharded over the GPUs; "
+                        "batched / linear / attention: the one-GPU forward + backward GEMM workloads "
+                        "(batched A[8,256,384] @ W[384,384]; linear layer X[16384,384] @ W[1536,384]^T + b; "
+                        "causal attention Q, K, V [64,6,256,64] with the softmax fused)")
     p.add_argument("--gather", choices=["fused", "nccl"], default="fused",
                    help="N>1: C rows reach every GPU from the GEMM epilogue over NVLink (fused) "
                         "or by an NCCL all-gather after it")
@@ -194,6 +197,8 @@ def main():
     args = parse_args()
     if args.workload == "decoder":
         return run_decoder(args)
+    if args.workload in ("batched", "linear", "attention"):
+        return run_small_workload(args)
     if args.impl == "reference":
         return run_reference_arm(args)
 
@@ -384,6 +389,138 @@ def main():
         "exchange_ms": gather_ms if world > 1 else 0.0,
         "clocks": clk,
     }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ small workloads
+def run_small_workload(args):
+    """One-GPU forward + backward GEMM workloads of the matmul path (the
+    parity configurations, timed): every GEMM through the library's public
+    API (functional.py). Each step is timed alone with CUDA events, L2 flushed
+    (a 512 MB write) between steps; GEMM-only time from events around each
+    library call. TFLOP/s against TF32 / 3 (3xTF32) or TF32; the attention
+    score product (HBM-bound) also as GB/s against the measured HBM rate."""
+    import torch
+
+    sys.path.insert(0, ROOT)
+    import macrograd_b200 as mg
+    from macrograd_b200 import _lib, functional as F
+
+    rank, local_rank, world = env_rank()
+    if world != 1:
+        print("the small workloads run on one GPU", file=sys.stderr)
+        return 2
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    lib = mg.load()
+    _lib.check(lib.mg_set_mode(_lib.MG_MODE_TF32X3 if args.mode == "3xtf32" else _lib.MG_MODE_TF32))
+    g = torch.Generator(device=dev)
+    g.manual_seed(20)
+    gemm_events = []
+
+    def timed(fn, *a, **k):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        r = fn(*a, **k)
+        e1.record()
+        gemm_events.append((e0, e1))
+        return r
+
+    if args.workload == "batched":
+        A = torch.empty(8, 256, 384, device=dev).uniform_(-1, 1, generator=g)
+        W = torch.empty(384, 384, device=dev).uniform_(-1, 1, generator=g)
+        dC = torch.ones(8, 256, 384, device=dev)
+        flops = 3 * 2.0 * 8 * 256 * 384 * 384
+        desc = {"workload": "batched fp32 matmul A[8,256,384] @ W[384,384], backward with dC = ones",
+                "gemms": "C = A W; dA = dC W^T; dW = A^T dC (batch folded into K = 2048)"}
+
+        def step():
+            timed(F.matmul, A, W)
+            timed(F.matmul_backward, A, W, dC)
+    elif args.workload == "linear":
+        bound = (6.0 / 384) ** 0.5
+        X = torch.empty(16384, 384, device=dev).uniform_(-1, 1, generator=g)
+        W = torch.empty(1536, 384, device=dev).uniform_(-bound, bound, generator=g)
+        b = torch.empty(1536, device=dev).uniform_(-bound, bound, generator=g)
+        dY = torch.empty(16384, 1536, device=dev).normal_(0, 1, generator=g)
+        flops = 3 * 2.0 * 16384 * 1536 * 384
+        desc = {"workload": "linear layer X[16384,384] @ W[1536,384]^T + b[1536], backward with dY ~ N(0,1)",
+                "gemms": "Y = X W^T + b (bias fused); dX = dY W; dW = dY^T X (transposed views in place)"}
+
+        def step():
+            timed(F.matmul, X, W, b, False, True)
+            timed(F.matmul_backward, X, W, dY, False, True)   # db = sum(dY) is not a GEMM
+    else:
+        Q = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 0.125, generator=g)
+        K = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 0.125, generator=g)
+        V = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 1, generator=g)
+        dO = torch.ones(64, 6, 256, 64, device=dev)
+        Qs = Q * 0.125
+        flops = 6 * 2.0 * 64 * 6 * 256 * 256 * 64
+        desc = {"workload": "causal attention Q, K, V [64,6,256,64]: P = softmax(Q K^T / 8 + causal) fused, "
+                            "O = P V, backward with dO = ones",
+                "gemms": "P (score product + mask + row softmax in the epilogue), O = P V, dP = dO V^T, "
+                         "dV = P^T dO, dQ/8 = dS K, dK = dS^T (Q/8); dS = P (dP - rowsum(P dP)) is not a GEMM "
+                         "(torch elementwise, in the step time, not in the GEMM time)"}
+
+        def step():
+            P = timed(F.attention_scores, Q, K, 0.125, True)
+            timed(F.matmul, P, V)
+            dP = timed(F.matmul, dO, V, None, False, True)
+            timed(F.matmul, P, dO, None, True, False)
+            dS = P * (dP - (P * dP).sum(-1, keepdim=True))
+            timed(F.matmul, dS, K)
+            timed(F.matmul, dS, Qs, None, True, False)
+
+    flush = torch.empty(128 * 1024 * 1024, device=dev)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    launches0 = lib.mg_launch_count()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    step_ms, gemm_ms, score_ms, each_ms = [], [], [], []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        gemm_events.clear()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        step_ms.append(e0.elapsed_time(e1))
+        gemm_ms.append(sum(a.elapsed_time(b) for a, b in gemm_events))
+        score_ms.append(gemm_events[0][0].elapsed_time(gemm_events[0][1]))
+        each_ms.append([a.elapsed_time(b) for a, b in gemm_events])
+    clk = clocks.stop()
+    launches = lib.mg_launch_count() - launches0
+    ms = statistics.mean(step_ms)
+    gms = statistics.mean(gemm_ms)
+    bf16, _, hbm, src = peaks()
+    peak = bf16 / 2.0 / (3.0 if args.mode == "3xtf32" else 1.0)
+    line = {
+        "metric": f"{args.workload} fwd+bwd GEMM TFLOP/s", "value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "gemm_ms_per_step": gms,
+        "step_tflops": flops / (ms * 1e-3) / 1e12, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch generator, seeded)",
+        "config": {**desc, "mode": args.mode, "gflop_per_step": flops / 1e9,
+                   "l2": "flushed between steps (512 MB write, untimed)"},
+        "roofline": {"bound": "tensor", "achieved": flops / (gms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": flops / (gms * 1e-3) / 1e12 / peak,
+                     "peak_source": f"{src} bf16 dense {bf16:.1f} / 2" + (" / 3" if args.mode == "3xtf32" else "")},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "per_call_ms": [statistics.mean(x) for x in zip(*each_ms)],
+    }
+    if args.workload == "attention":
+        sbytes = 4.0 * (2 * 64 * 6 * 256 * 64 + 64 * 6 * 256 * 256)
+        sms = statistics.mean(score_ms)
+        line["score_product"] = {"bound": "hbm", "ms": sms, "achieved": sbytes / (sms * 1e-3) / 1e9, "peak": hbm,
+                                 "unit": "GB/s", "frac": sbytes / (sms * 1e-3) / 1e9 / hbm,
+                                 "bytes": sbytes, "note": "Q, K read + P written, one fused launch"}
     print(json.dumps(line), flush=True)
     return 0
 

@@ -49,6 +49,7 @@ struct DeviceState {
     size_t attr_smem[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // dynamic smem opted in, per kernel variant
     int max_clusters[4] = {0, 0, 0, 0};               // resident CTA pairs, per pair-kernel tile width
     int* status = nullptr;   // device address of g_device_status
+    cudaMemPool_t pool = nullptr;   // the library's own stream-ordered pool (workspace)
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -143,6 +144,17 @@ mg_status device_state(DeviceState** out)
                     return fail(MG_ERR_CUDA, "cuTensorMapEncodeTiled not available from the driver");
                 g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
             }
+            // Workspace (K-split partials, re-laid-out operands) comes from a
+            // pool of the library's own that keeps its memory between calls:
+            // the device's default pool would hand it back at every
+            // synchronisation and re-map it on the next call.
+            cudaMemPoolProps pp = {};
+            pp.allocType = cudaMemAllocationTypePinned;
+            pp.location.type = cudaMemLocationTypeDevice;
+            pp.location.id = dev;
+            MG_CUDA_TRY(cudaMemPoolCreate(&d.pool, &pp));
+            uint64_t keep = ~0ull;
+            MG_CUDA_TRY(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
             d.ready = true;
         }
     }
@@ -338,6 +350,7 @@ __global__ void k0_fill_kernel(FillParams p)
 // pieces of that fixed buffer instead and never allocates or frees.
 struct Workspace {
     void* stream;
+    cudaMemPool_t pool = nullptr;
     void* ptrs[8] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
     int n = 0;
     uint8_t* arena = nullptr;
@@ -360,7 +373,7 @@ struct Workspace {
         }
         void* p = nullptr;
         if (g_alloc) p = g_alloc(bytes, stream, g_alloc_ctx);
-        else if (cudaMallocAsync(&p, bytes, (cudaStream_t)stream) != cudaSuccess) p = nullptr;
+        else if (cudaMallocFromPoolAsync(&p, bytes, pool, (cudaStream_t)stream) != cudaSuccess) p = nullptr;
         if (p) ptrs[n++] = p;
         return p;
     }
@@ -546,7 +559,9 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             dev->max_clusters[slot - 4] = std::max(1, std::min(n, dev->sm_count / 2));
         }
         const int resident = dev->max_clusters[slot - 4];
-        if (setup_split<BN>(gp, resident, ws, st, allow_split)) {
+        const bool split_k = setup_split<BN>(gp, resident, ws, st, allow_split);
+        gp.dbuf = (!split_k && gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
+        if (split_k) {
             // the final K-ranges wait for partials from other CTAs of the grid:
             // launch it cooperatively, so every CTA is resident at once
             cudaLaunchAttribute attr2[2] = {attr[0], {}};
@@ -562,6 +577,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             (void)cudaGetLastError();   // not launchable cooperatively here: run unsplit
             gp.full_tiles = gp.total_tiles;
             gp.nlev = 0;
+            gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
         }
@@ -569,7 +585,9 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
         MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm));
     } else {
-        if (setup_split<BN>(gp, dev->sm_count, ws, st, allow_split)) {
+        const bool split_k = setup_split<BN>(gp, dev->sm_count, ws, st, allow_split);
+        gp.dbuf = (!split_k && gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
+        if (split_k) {
             cudaLaunchConfig_t cfg = {};
             cfg.gridDim = dim3((unsigned)dev->sm_count, 1, 1);
             cfg.blockDim = dim3(mg::kThreads, 1, 1);
@@ -587,6 +605,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             (void)cudaGetLastError();
             gp.full_tiles = gp.total_tiles;
             gp.nlev = 0;
+            gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
         }
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
         k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, gp, pm);
@@ -779,6 +798,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
 
     Workspace ws;
     ws.stream = stream;
+    ws.pool = dev->pool;
     ws.arena = arena;
     ws.arena_cap = arena_cap;
     BatchMap am, bmp;

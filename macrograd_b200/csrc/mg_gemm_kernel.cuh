@@ -110,6 +110,7 @@ struct GemmParams {
     int relay_spin;             // split warps poll without suspend hints
     int split;                  // 1 = 3xTF32
     int presplit;               // 3xTF32 with lo planes precomputed in HBM (tmAlo / tmBlo)
+    int dbuf;                   // every unit is one chunk: two accumulators, no promotion
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
     int a_rank, b_rank;         // tensor-map ranks (2 + mapped batch dims)
     uint32_t idesc;
@@ -238,8 +239,11 @@ struct SharedState {
     uint64_t empty[kMaxStages];       // local: the MMAs reading the stage are done
     uint64_t part_full;               // local: partial accumulator complete
     uint64_t part_free;               // MMA issuer's CTA: every epilogue took the partial
-    uint64_t master_done;             // local (softmax): every epilogue thread wrote its master half
-    uint64_t master_free;             // local (softmax): warps 0-3 finished reading the master
+    uint64_t part_full1;              // the same for the second accumulator (p.dbuf)
+    uint64_t part_free1;
+    uint64_t row_max;                 // local (softmax): every epilogue thread posted its half-row max
+    uint64_t row_sum;                 // local (softmax): ... its half-row sum
+    uint64_t row_read;                // local (softmax): ... read its partner's sum
     uint64_t drain;
     uint32_t tmem_base;
     volatile int abort_flag;
@@ -579,8 +583,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_init(smem_u32(&ss->part_full), 1);
         mbar_init(smem_u32(&ss->part_free), kEpiThreads * (kPair ? 2 : 1));
-        mbar_init(smem_u32(&ss->master_done), kEpiThreads);
-        mbar_init(smem_u32(&ss->master_free), kEpiThreads / 2);
+        mbar_init(smem_u32(&ss->part_full1), 1);
+        mbar_init(smem_u32(&ss->part_free1), kEpiThreads * (kPair ? 2 : 1));
+        mbar_init(smem_u32(&ss->row_max), kEpiThreads);
+        mbar_init(smem_u32(&ss->row_sum), kEpiThreads);
+        mbar_init(smem_u32(&ss->row_read), kEpiThreads);
         mbar_init(smem_u32(&ss->drain), 1);
         ss->abort_flag = 0;
         ss->tiles_stored = 0u;
@@ -611,6 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // barriers of the MMA issuer's CTA, as shared::cluster addresses
     const uint32_t split_done0 = kPair ? cluster_map(smem_u32(&ss->split_done[0]), 0) : smem_u32(&ss->split_done[0]);
     const uint32_t part_free0 = kPair ? cluster_map(smem_u32(&ss->part_free), 0) : smem_u32(&ss->part_free);
+    const uint32_t part_free1_0 = kPair ? cluster_map(smem_u32(&ss->part_free1), 0) : smem_u32(&ss->part_free1);
 
     if (warp == kProducerWarp) {
         // ------------------------------------------------ TMA producer
@@ -693,7 +701,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t b_lay = p.b_mn ? kLayoutSw128Base32 : kLayoutSw128;
             const uint32_t a_kstep = p.a_mn ? 1024u : 32u;
             const uint32_t b_kstep = p.b_mn ? 1024u : 32u;
-            const uint32_t d_tmem = tmem_base;   // partial accumulator, columns [0, BN)
+            uint32_t d_tmem = tmem_base;   // accumulator: the partial, columns [0, BN)
             auto mma = [&](uint64_t da, uint64_t db, uint32_t acc) {
                 if (kPair) tc_mma_tf32_pair(d_tmem, da, db, p.idesc, acc);
                 else tc_mma_tf32(d_tmem, da, db, p.idesc, acc);
@@ -708,14 +716,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool ok = true;
             Unit u;
             for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+                // p.dbuf: whole tiles of one chunk alternate between the two
+                // accumulators, so a tile's MMAs run during the previous
+                // tile's epilogue
+                const int rg = p.dbuf ? (ui & 1) : 0;
+                d_tmem = tmem_base + (uint32_t)(rg * BN);
+                const uint32_t acc_free = smem_u32(rg ? &ss->part_free1 : &ss->part_free);
+                const uint32_t acc_full = smem_u32(rg ? &ss->part_full1 : &ss->part_full);
                 for (int kb = u.kb0; kb < u.kb1; ++kb) {
                     const int rel = kb - u.kb0;   // chunks restart with every unit
                     const bool chunk_start = (rel % p.chunk_kb) == 0;
                     const bool chunk_end = (rel % p.chunk_kb) == p.chunk_kb - 1 || kb == u.kb1 - 1;
                     if (chunk_start) {
-                        // every epilogue has taken the previous partial
-                        if (!wait_phase<kPair ? 2 : 0>(smem_u32(&ss->part_free), chunk_phase ^ 1u, ss, p,
-                                                       kWaitMmaPartialFree)) {
+                        // every epilogue has taken the previous partial (p.dbuf: has
+                        // finished with this accumulator two tiles ago)
+                        const uint32_t fpar = p.dbuf ? ((((uint32_t)ui >> 1) & 1u) ^ 1u) : (chunk_phase ^ 1u);
+                        if (!wait_phase<kPair ? 2 : 0>(acc_free, fpar, ss, p, kWaitMmaPartialFree)) {
                             ok = false;
                             break;
                         }
@@ -744,7 +760,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     commit_all(smem_u32(&ss->empty[stage]));   // frees the stage in every CTA
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
                     if (chunk_end) {
-                        commit_all(smem_u32(&ss->part_full));  // partial ready for promotion
+                        commit_all(acc_full);  // partial ready for promotion (p.dbuf: for the output)
                         chunk_phase ^= 1u;
                     }
                 }
@@ -854,23 +870,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool has_bias = (p.epi & kEpiBias) != 0;
         const bool softmax = (p.epi & kEpiSoftmax) != 0;
         uint32_t chunk_phase = 0;
-        uint32_t md_phase = 0;
-        uint32_t mf_phase = 0;
+        uint32_t row_phase = 0;   // softmax: one phase of row_max / row_sum / row_read per tile
         bool ok = true;
         Unit u;
         for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
             const TileCoord tc = decode_tile(u.tile, p);
             const int n_chunks = (u.kb1 - u.kb0 + p.chunk_kb - 1) / p.chunk_kb;
-            if (softmax && half == 1) {
-                // warps 0-3 read the whole master row of the previous tile; do
-                // not overwrite this half before they are done with it
-                const bool freed = wait_phase<1>(smem_u32(&ss->master_free), mf_phase ^ 1u, ss, p,
-                                                 kWaitEpilogueMasterFree);
-                if (!__all_sync(0xffffffffu, freed)) break;
-                mf_phase ^= 1u;
+            const int rg = p.dbuf ? (ui & 1) : 0;
+            if (p.dbuf) {
+                // one chunk: the accumulator itself is the result
+                const bool got = wait_phase<1>(smem_u32(rg ? &ss->part_full1 : &ss->part_full),
+                                               ((uint32_t)ui >> 1) & 1u, ss, p, kWaitEpiloguePartial);
+                if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+                tc_fence_after();
             }
             // ---- promotions: master = sum of the tile's partials (fp32 round-to-nearest)
-            for (int c = 0; c < n_chunks; ++c) {
+            for (int c = 0; c < (p.dbuf ? 0 : n_chunks); ++c) {
                 const bool got = wait_phase<1>(smem_u32(&ss->part_full), chunk_phase, ss, p, kWaitEpiloguePartial);
                 if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                 tc_fence_after();
@@ -899,14 +914,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 chunk_phase ^= 1u;
             }
             if (!ok) break;
-            if (softmax) {
-                // every epilogue thread of this CTA has written its master columns
-                mbar_arrive(smem_u32(&ss->master_done));
-                const bool synced = wait_phase<1>(smem_u32(&ss->master_done), md_phase, ss, p, kWaitEpilogueMaster);
-                md_phase ^= 1u;
-                if (!__all_sync(0xffffffffu, synced)) break;
-                tc_fence_after();
-            }
 
             if (u.kind == 1) {
                 // A partial K-range: the master goes to its workspace slot for
@@ -959,59 +966,71 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t crow_idx = rok ? gm + (p.export_peers ? p.peer_row0 : 0) : 0;
             float* crow = p.C + coff + crow_idx * p.ldc;
             const float* brow = has_bias ? p.bias + boff + (int64_t)(rok ? gm : 0) * p.bias_rs : nullptr;
-            const uint32_t t_row = lane_base + (uint32_t)BN;   // master, column 0
+            // the result, column 0: the master, or (p.dbuf) this tile's accumulator
+            const uint32_t t_row = lane_base + (uint32_t)(p.dbuf ? rg * BN : BN);
 
             if (softmax) {
-                // Warps 0-3: one thread owns one full row (N <= BN, single
-                // n-tile), so the row softmax needs no cross-thread reduction.
-                if (half == 0) {
-                    const bool causal = (p.epi & kEpiCausal) != 0;
-                    float mx = -INFINITY;
-                    for (int c = 0; c < BN && c < p.N; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld32(t_row + c, r);
+                // Row softmax (N <= BN, one n-tile). A row lives in one TMEM
+                // lane; warp w and its partner w ^ 4 hold its two column
+                // halves. Each thread reduces its half, the halves meet
+                // through the warps' staging blocks (bounded mbarrier waits),
+                // exp(x - max) goes back into the master once, then the scaled
+                // values leave. Semantics of Tensor::softmax: max, exp, sum,
+                // divide (here: multiply by the rounded reciprocal).
+                const bool causal = (p.epi & kEpiCausal) != 0;
+                float* xch = stage_w;                                                    // my posts
+                const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;   // partner's
+                auto logit = [&](uint32_t bits, int gn) {
+                    float x = p.alpha * __uint_as_float(bits);
+                    if (has_bias && rok) x += brow[(int64_t)gn * p.bias_cs];
+                    if (causal && gn > gm) x = -INFINITY;
+                    return x;
+                };
+                // every epilogue thread of the CTA has arrived on `bar` this tile
+                auto rows_meet = [&](uint64_t* bar) {
+                    mbar_arrive(smem_u32(bar));
+                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueMaster);
+                    return __all_sync(0xffffffffu, met);
+                };
+                float mx = -INFINITY;
+                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_row + c, r);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int gn = c + j;
-                            if (gn < p.N) {
-                                float v = p.alpha * __uint_as_float(r[j]);
-                                if (has_bias && rok) v += brow[(int64_t)gn * p.bias_cs];
-                                if (causal && gn > gm) v = -INFINITY;
-                                mx = fmaxf(mx, v);
-                            }
-                        }
-                    }
-                    float sum = 0.f;
-                    for (int c = 0; c < BN && c < p.N; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld32(t_row + c, r);
+                    for (int j = 0; j < 32; ++j)
+                        if (c + j < p.N) mx = fmaxf(mx, logit(r[j], c + j));
+                }
+                xch[lane] = mx;
+                if (!rows_meet(&ss->row_max)) { ok = false; break; }
+                mx = fmaxf(mx, pxch[lane]);
+                float sum = 0.f;
+                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_row + c, r);
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int gn = c + j;
-                            if (gn < p.N) {
-                                float v = p.alpha * __uint_as_float(r[j]);
-                                if (has_bias && rok) v += brow[(int64_t)gn * p.bias_cs];
-                                if (causal && gn > gm) v = -INFINITY;
-                                sum += expf(v - mx);
-                            }
-                        }
+                    for (int j = 0; j < 32; ++j) {
+                        const float x = c + j < p.N ? logit(r[j], c + j) : -INFINITY;
+                        const float e = x == -INFINITY ? 0.f : expf(x - mx);
+                        sum += e;
+                        r[j] = __float_as_uint(e);
                     }
-                    for (int c = 0; c < BN && c < p.N; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld32(t_row + c, r);
-                        float v[32];
+                    tmem_st32(t_row + c, r);
+                }
+                xch[32 + lane] = sum;
+                if (!rows_meet(&ss->row_sum)) { ok = false; break; }
+                // the row's sum: first half's columns, then the second half's
+                sum = half ? pxch[32 + lane] + sum : sum + pxch[32 + lane];
+                // the partner has read this block before the stores reuse it
+                if (!rows_meet(&ss->row_read)) { ok = false; break; }
+                row_phase ^= 1u;
+                const float inv = 1.f / sum;
+                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_row + c, r);
+                    float v[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int gn = c + j;
-                            float x = p.alpha * __uint_as_float(r[j]);
-                            if (gn < p.N && has_bias && rok) x += brow[(int64_t)gn * p.bias_cs];
-                            if (causal && gn > gm) x = -INFINITY;
-                            v[j] = expf(x - mx) / sum;
-                        }
-                        store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
-                    }
-                    tc_fence_before();
-                    mbar_arrive(smem_u32(&ss->master_free));
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
+                    store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
                 }
             } else {
                 for (int c = 32 * c_lo; c < 32 * c_hi; c += 32) {
@@ -1037,6 +1056,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
+            if (p.dbuf) {
+                // done with this accumulator: the MMAs of the tile after next may use it
+                if (kPair) mbar_arrive_cluster(rg ? part_free1_0 : part_free0);
+                else mbar_arrive(smem_u32(rg ? &ss->part_free1 : &ss->part_free));
+            }
             if (p.export_peers) {
                 // this warp's part of the tile is in C (visible GPU-wide) for the export warps
                 __threadfence();
