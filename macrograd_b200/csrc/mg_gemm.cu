@@ -499,13 +499,17 @@ template <int BN>
 bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, bool allow)
 {
     const int nslots = allow ? plan_split(gp, units) : 0;
+    gp.tail_share = 0;
     if (nslots == 0) {
         gp.full_tiles = gp.total_tiles;
         gp.nlev = 0;
         return false;
     }
     const size_t part = (size_t)nslots * 2 * mg::kBM * BN * sizeof(float);
-    const size_t flags = (size_t)nslots * 2 * sizeof(unsigned int);
+    // fused all-gather: a counter per last-level tile half, for the shared export
+    const bool tail = gp.export_peers && gp.npeers > 0 && tuning_int("MG_GEMM_TAIL_SHARE", 1, 0, 1);
+    const size_t nflags = (size_t)nslots * 2 + (tail ? (size_t)gp.lev_tiles[gp.nlev - 1] * 2 : 0);
+    const size_t flags = nflags * sizeof(unsigned int);
     uint8_t* w = static_cast<uint8_t*>(ws ? ws->get(part + flags) : nullptr);
     if (!w || cudaMemsetAsync(w + part, 0, flags, st) != cudaSuccess) {
         gp.full_tiles = gp.total_tiles;
@@ -514,6 +518,8 @@ bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, 
     }
     gp.part_ws = reinterpret_cast<float*>(w);
     gp.part_flag = reinterpret_cast<unsigned int*>(w + part);
+    gp.tail_share = tail ? 1 : 0;
+    gp.tail_flag = gp.part_flag + (size_t)nslots * 2;
     return true;
 }
 
@@ -577,6 +583,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             (void)cudaGetLastError();   // not launchable cooperatively here: run unsplit
             gp.full_tiles = gp.total_tiles;
             gp.nlev = 0;
+            gp.tail_share = 0;
             gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
@@ -605,6 +612,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             (void)cudaGetLastError();
             gp.full_tiles = gp.total_tiles;
             gp.nlev = 0;
+            gp.tail_share = 0;
             gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
         }
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
@@ -930,6 +938,8 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
             if (q != local) gp.peers[gp.npeers++] = scatter->peers[q];
         }
         gp.export_vec = vec ? 1 : 0;
+        gp.export_threads = tuning_int("MG_GEMM_EXPORT_WARPS", 2, 1, 2) * 32;
+        gp.export_stream = tuning_int("MG_GEMM_EXPORT_STREAM", 0, 0, 1);
     } else if (scatter) {
         gp.npeers = scatter->npeers;
         gp.peer_row0 = scatter->row0;

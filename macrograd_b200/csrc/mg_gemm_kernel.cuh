@@ -151,6 +151,14 @@ struct GemmParams {
     int lev_split[kMaxLevels], lev_tiles[kMaxLevels], lev_tile0[kMaxLevels], lev_slot0[kMaxLevels];
     float* part_ws;             // [slot][cta rank][BN/32 chunks][128 rows][32] floats
     unsigned int* part_flag;    // [slot][cta rank]: epilogue warps that stored their part
+    // Fused all-gather with split levels: the last level's tiles finish last,
+    // so every CTA's export warps (not only the owners') send a share of
+    // their rows, each once its tile half is in C (tail_flag[tile][cta rank]
+    // counts the owner's epilogue warps).
+    int tail_share;
+    unsigned int* tail_flag;
+    int export_threads;         // export threads in use (32 or 64)
+    int export_stream;          // remote 16-byte stores with the streaming (evict-first) hint
 };
 
 // 2-D tensor maps over every rank's full C (fused all-gather with TMA stores).
@@ -428,17 +436,19 @@ template <bool kVec>
 __device__ __forceinline__ void export_tile(const GemmParams& p, int64_t off, int rows, int cols, int et)
 {
     constexpr int kUnroll = 8;
+    const int nt = p.export_threads;
+    if (et >= nt) return;
     const float* src = p.C + off;
     if (kVec) {
         const int c4 = cols >> 2;
         const int items = rows * c4;
 #pragma unroll 1
-        for (int base = et; base < items; base += kExportThreads * kUnroll) {
+        for (int base = et; base < items; base += nt * kUnroll) {
             float4 v[kUnroll];
             int64_t eo[kUnroll];
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
-                const int i = base + u * kExportThreads;
+                const int i = base + u * nt;
                 const int r = i / c4;
                 eo[u] = (int64_t)r * p.ldc + 4 * (i - r * c4);
                 if (i < items) v[u] = __ldcg(reinterpret_cast<const float4*>(src + eo[u]));
@@ -447,19 +457,23 @@ __device__ __forceinline__ void export_tile(const GemmParams& p, int64_t off, in
             for (int q = 0; q < p.npeers; ++q) {
                 float* dst = p.peers[q] + off;
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u)
-                    if (base + u * kExportThreads < items) *reinterpret_cast<float4*>(dst + eo[u]) = v[u];
+                for (int u = 0; u < kUnroll; ++u) {
+                    if (base + u * nt >= items) continue;
+                    float4* d4 = reinterpret_cast<float4*>(dst + eo[u]);
+                    if (p.export_stream) __stcs(d4, v[u]);   // evict-first at the destination
+                    else *d4 = v[u];
+                }
             }
         }
     } else {
         const int items = rows * cols;
 #pragma unroll 1
-        for (int base = et; base < items; base += kExportThreads * kUnroll) {
+        for (int base = et; base < items; base += nt * kUnroll) {
             float v[kUnroll];
             int64_t eo[kUnroll];
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
-                const int i = base + u * kExportThreads;
+                const int i = base + u * nt;
                 const int r = i / cols;
                 eo[u] = (int64_t)r * p.ldc + (i - r * cols);
                 if (i < items) v[u] = __ldcg(src + eo[u]);
@@ -469,7 +483,7 @@ __device__ __forceinline__ void export_tile(const GemmParams& p, int64_t off, in
                 float* dst = p.peers[q] + off;
 #pragma unroll
                 for (int u = 0; u < kUnroll; ++u)
-                    if (base + u * kExportThreads < items) dst[eo[u]] = v[u];
+                    if (base + u * nt < items) dst[eo[u]] = v[u];
             }
         }
     }
@@ -783,6 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_count(&ss->tiles_stored, (unsigned int)kEpiWarps * (j + 1u), ss, p, kWaitExportTile))
                     break;
                 if (u.kind == 1) continue;   // a partial K-range: its tile leaves with the final range
+                if (p.tail_share && u.tile >= p.lev_tile0[p.nlev - 1]) continue;   // shared below
                 __threadfence();
                 const TileCoord tc = decode_tile(u.tile, p);
                 int idx[kMaxBatchDims];
@@ -799,6 +814,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int64_t off = coff + (p.peer_row0 + m0) * p.ldc + n0;
                 if (p.export_vec) export_tile<true>(p, off, rows, cols, et);
                 else export_tile<false>(p, off, rows, cols, et);
+            }
+            if (p.tail_share) {
+                // this CTA's share of the last level's rows (every CTA of the grid)
+                constexpr int kHalves = kPair ? 2 : 1;
+                const int t0 = p.lev_tile0[p.nlev - 1];
+                const int R = p.lev_tiles[p.nlev - 1] * kHalves * kBM;
+                const int G = (int)gridDim.x, b = (int)blockIdx.x;
+                const int r_end = (int)((int64_t)R * (b + 1) / G);
+                for (int r = (int)((int64_t)R * b / G); r < r_end;) {
+                    const int piece = r / kBM;   // (tile, half) of the level
+                    const int cnt = min(r_end, (piece + 1) * kBM) - r;
+                    if (!wait_count(&p.tail_flag[piece], (unsigned int)kEpiWarps, ss, p, kWaitExportTile)) break;
+                    __threadfence();
+                    const TileCoord tc = decode_tile(t0 + piece / kHalves, p);
+                    int idx[kMaxBatchDims];
+                    batch_index(tc.batch, p, idx);
+                    int64_t coff = 0;
+#pragma unroll
+                    for (int d = 0; d < kMaxBatchDims; ++d)
+                        if (d < p.nbd) coff += (int64_t)idx[d] * p.c_bs[d];
+                    const int m0 = tc.mt * L::kTileRows + (piece % kHalves) * kBM + (r - piece * kBM);
+                    const int n0 = tc.nt * BN;
+                    const int rows = min(cnt, p.M - m0);
+                    const int cols = min(BN, p.N - n0);
+                    if (rows > 0 && cols > 0) {
+                        const int64_t off = coff + (p.peer_row0 + m0) * p.ldc + n0;
+                        if (p.export_vec) export_tile<true>(p, off, rows, cols, et);
+                        else export_tile<false>(p, off, rows, cols, et);
+                    }
+                    r += cnt;
+                }
             }
             // the peers' rows have landed before the kernel is seen as complete
             __threadfence_system();
@@ -1056,6 +1102,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
+            if (p.tail_share && u.kind == 2 && u.tile >= p.lev_tile0[p.nlev - 1]) {
+                // a last-level tile half is in C: any CTA's export warps may send it
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(&p.tail_flag[(u.tile - p.lev_tile0[p.nlev - 1]) * (kPair ? 2 : 1) + (int)rank], 1u);
+            }
             if (p.dbuf) {
                 // done with this accumulator: the MMAs of the tile after next may use it
                 if (kPair) mbar_arrive_cluster(rg ? part_free1_0 : part_free0);

@@ -3,7 +3,9 @@ into the GEMM kernel and the NCCL all-gather both leave the full C on every
 GPU, matching the oracle on sampled rows of each rank's block. The fused path
 runs in both of its forms: export warps copying finished tiles to the peer
 (default) and the epilogue storing to every rank itself (MG_GEMM_EXPORT=0);
-a 1001-wide C takes the 4-byte copy paths. Skipped when fewer than 2 GPUs are
+with the K split forced (MG_GEMM_SPLIT_MIN_KB=1) the last split level's rows
+go out through every CTA's export warps; a 1001-wide C takes the 4-byte copy
+paths. The NCCL gather of the same kernel's rows must be bit-identical. Skipped when fewer than 2 GPUs are
 visible."""
 import os
 import socket
@@ -49,9 +51,12 @@ def _worker(rank, world, port, n, q):
         A_local = torch.from_numpy(A[r0:r1].copy()).to(dev)
         Bg = torch.from_numpy(B).to(dev)
         report = {}
-        for mode, export in ((_lib.MG_MODE_TF32X3, "1"), (_lib.MG_MODE_TF32, "1"), (_lib.MG_MODE_TF32X3, "0")):
+        # (mode, export warps, K-split allowed down to this many K-blocks per range)
+        for mode, export, min_kb in ((_lib.MG_MODE_TF32X3, "1", "16"), (_lib.MG_MODE_TF32, "1", "16"),
+                                     (_lib.MG_MODE_TF32X3, "0", "16"), (_lib.MG_MODE_TF32X3, "1", "1")):
             lib.mg_set_mode(mode)
             os.environ["MG_GEMM_EXPORT"] = export
+            os.environ["MG_GEMM_SPLIT_MIN_KB"] = min_kb
             full = torch.full((n, n), float("nan"), device=dev)
             peers = PeerRows(full)
             for _ in range(2):                       # two calls in a row into the same buffers
@@ -66,7 +71,7 @@ def _worker(rank, world, port, n, q):
             rows = [0, 5, n // 2 - 1, n // 2, n // 2 + 7, n - 1]
             ref = ob.oracle_matmul(A[rows], B)
             tol = 1e-5 if mode == _lib.MG_MODE_TF32X3 else 2e-3
-            report[(mode, export)] = (bool(np.all(np.isfinite(got))), ob.frob_rel_err(got[rows], ref) <= tol,
+            report[(mode, export, min_kb)] = (bool(np.all(np.isfinite(got))), ob.frob_rel_err(got[rows], ref) <= tol,
                             bool(np.array_equal(got, full_nccl.cpu().numpy())))
             dist.barrier()
             peers.close()
@@ -95,8 +100,8 @@ def test_fused_all_gather_on_two_gpus(n):
         p.join(timeout=60)
     for rank, rep in results.items():
         assert isinstance(rep, dict), f"rank {rank}: {rep}"
-        for (mode, export), (finite, close, same) in rep.items():
-            what = f"rank {rank} mode {mode} export {export}"
+        for (mode, export, min_kb), (finite, close, same) in rep.items():
+            what = f"rank {rank} mode {mode} export {export} split min_kb {min_kb}"
             assert finite, f"{what}: C has rows nobody wrote"
             assert close, f"{what}: rows differ from the oracle"
             assert same, f"{what}: fused and NCCL all-gather differ"
