@@ -126,6 +126,18 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
                             int32_t rank, int32_t trans_a, int32_t trans_b,
                             float alpha, int32_t causal, void* stream);
 
+/* Fused softmax backward (no counterpart in the reference, which runs it as
+ * a separate pass, tensor_ops.cpp:2056-2059): with G = alpha * op(A) op(B)
+ * the upstream gradient of a row softmax whose output is P,
+ *     dS = P * (G - rowsum(P * G)),
+ * e.g. the attention backward's dP = dO V^T (A = dO, B = V, trans_b = 1)
+ * followed by the softmax derivative, in one launch. P has out's shape and is
+ * contiguous like out. Shapes as mg_matmul. Requires N <= 256. */
+mg_status mg_matmul_softmax_backward(float* dS, const float* A, const float* B, const float* P,
+                                     const int32_t* out_shape, const int32_t* A_shape,
+                                     const int32_t* B_shape, int32_t rank, int32_t trans_a,
+                                     int32_t trans_b, float alpha, void* stream);
+
 /* ---- multi-GPU: row-sharded GEMM with the all-gather fused into it ------
  * No counterpart in the reference (single-GPU only, README.md:538). A job of
  * R ranks (one process per GPU) splits the rows of A (and of C) into R blocks;

@@ -82,6 +82,8 @@ SIGNATURES = {
     "mg_matmul_bias": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
     "mg_matmul_softmax": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32P, _I32, _I32, _I32,
                                          ctypes.c_float, _I32, _P]),
+    "mg_matmul_softmax_backward": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32,
+                                                  ctypes.c_float, _P]),
     "mg_matmul_noalloc": (ctypes.c_int, [_P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
     "mg_gemm_scatter_rows": (ctypes.c_int, [ctypes.POINTER(GemmDesc), _P, _P, _P, ctypes.POINTER(_P), _I32,
                                             ctypes.c_int64, ctypes.c_int64, _P]),

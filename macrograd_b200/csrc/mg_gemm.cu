@@ -664,10 +664,11 @@ bool want_presplit(double flops, int64_t m_tiles, int64_t n_tiles)
 int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, const DeviceState* dev)
 {
     const int forced = tuning_int("MG_GEMM_BN", 0, 64, 256);
-    const bool fits = !(d->epilogue & MG_EPI_SOFTMAX) || d->N <= forced;   // softmax: one tile per row
+    const bool row_epi = (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) != 0;
+    const bool fits = !row_epi || d->N <= forced;   // softmax: one tile per row
     if (fits && (forced == 64 || forced == 128 || forced == 256 || (forced == 224 && pair))) return forced;
     const int base = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
-    if (!pair || base != 256 || (d->epilogue & MG_EPI_SOFTMAX)) return base;
+    if (!pair || base != 256 || row_epi) return base;
     const int64_t m_tiles = (d->M + 2 * mg::kBM - 1) / (2 * mg::kBM);
     const int64_t units = std::max(1, dev->sm_count / 2);
     auto cost = [&](int bn) {
@@ -696,8 +697,10 @@ mg_status validate(const mg_gemm_desc* d, float* C, const float* A, const float*
         if (d->batch[i] < 0) return fail(MG_ERR_INVALID, "negative batch size at dim %d", i);
     if (d->mode != MG_MODE_DEFAULT && d->mode != MG_MODE_TF32X3 && d->mode != MG_MODE_TF32)
         return fail(MG_ERR_INVALID, "unknown mode %d", d->mode);
-    if (d->epilogue & ~(MG_EPI_BIAS | MG_EPI_CAUSAL | MG_EPI_SOFTMAX))
+    if (d->epilogue & ~(MG_EPI_BIAS | MG_EPI_CAUSAL | MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd))
         return fail(MG_ERR_INVALID, "unknown epilogue flags 0x%x", d->epilogue);
+    if ((d->epilogue & mg::kEpiSoftmaxBwd) && (d->epilogue != mg::kEpiSoftmaxBwd || d->N > 256 || d->beta != 0.f))
+        return fail(MG_ERR_INVALID, "the softmax-backward epilogue stands alone, with N <= 256 and beta 0");
     if ((d->epilogue & MG_EPI_CAUSAL) && !(d->epilogue & MG_EPI_SOFTMAX))
         return fail(MG_ERR_INVALID, "MG_EPI_CAUSAL requires MG_EPI_SOFTMAX");
     if ((d->epilogue & MG_EPI_SOFTMAX) && d->N > 256)
@@ -753,11 +756,13 @@ struct ScatterSpec {
 
 static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, const float* B,
                            const float* bias, void* stream, uint8_t* arena, size_t arena_cap,
-                           const ScatterSpec* scatter = nullptr)
+                           const ScatterSpec* scatter = nullptr, const float* aux = nullptr)
 {
     g_last_error.clear();
     mg_status s = validate(d, C, A, B, bias);
     if (s != MG_OK) return s;
+    if ((d->epilogue & mg::kEpiSoftmaxBwd) && !aux)
+        return fail(MG_ERR_INVALID, "the softmax-backward epilogue needs P (mg_matmul_softmax_backward)");
     cudaStream_t st = (cudaStream_t)stream;
     int64_t nbatch = 1;
     for (int i = 0; i < d->batch_rank; ++i) nbatch *= d->batch[i];
@@ -910,6 +915,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.C = C;
     gp.ldc = d->ldc;
     gp.bias = has_bias ? bias : nullptr;
+    gp.aux = aux;
     gp.bias_rs = d->bias_rs;
     gp.bias_cs = d->bias_cs;
     gp.alpha = d->alpha;
@@ -965,8 +971,8 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
         }
     }
 
-    // the row softmax needs whole rows in one tile: no K split there
-    const bool allow_split = (d->epilogue & MG_EPI_SOFTMAX) == 0;
+    // the row softmax (and its backward) needs whole rows in one tile: no K split there
+    const bool allow_split = (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) == 0;
     if (pair) {
         switch (bn) {
         case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
@@ -1087,6 +1093,20 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
     d.alpha = alpha;
     d.epilogue = MG_EPI_SOFTMAX | (bias ? MG_EPI_BIAS : 0) | (causal ? MG_EPI_CAUSAL : 0);
     return mg_gemm(&d, out, A, B, bias, stream);
+}
+
+mg_status mg_matmul_softmax_backward(float* dS, const float* A, const float* B, const float* P,
+                                     const int32_t* out_shape, const int32_t* A_shape, const int32_t* B_shape,
+                                     int32_t rank, int32_t trans_a, int32_t trans_b, float alpha, void* stream)
+{
+    g_last_error.clear();
+    if (!P) return fail(MG_ERR_INVALID, "P is NULL");
+    mg_gemm_desc d;
+    mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, nullptr, rank, trans_a, trans_b);
+    if (s != MG_OK) return s;
+    d.alpha = alpha;
+    d.epilogue = mg::kEpiSoftmaxBwd;
+    return gemm_impl(&d, dS, A, B, nullptr, stream, nullptr, 0, nullptr, P);
 }
 
 // mg_matmul without any allocation: the only scratch it may need (the padded

@@ -83,7 +83,7 @@ constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitim
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
 constexpr uint32_t kSleepHintNs = 20000u;          // try_wait suspend hint
 
-enum : int { kEpiBias = 1, kEpiCausal = 2, kEpiSoftmax = 4 };
+enum : int { kEpiBias = 1, kEpiCausal = 2, kEpiSoftmax = 4, kEpiSoftmaxBwd = 8 };
 
 // Wait sites, reported in the status detail word when a wait gives up.
 enum : int {
@@ -122,6 +122,7 @@ struct GemmParams {
     int64_t ldc;
     int64_t c_bs[kMaxBatchDims];
     const float* bias;
+    const float* aux;           // kEpiSoftmaxBwd: the softmax output P, laid out like C
     int64_t bias_rs, bias_cs;
     int64_t bias_bs[kMaxBatchDims];
     float alpha, beta;
@@ -915,6 +916,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          warp * kStageFloatsPerWarp;                  // this warp's store staging block
         const bool has_bias = (p.epi & kEpiBias) != 0;
         const bool softmax = (p.epi & kEpiSoftmax) != 0;
+        const bool softmax_bwd = (p.epi & kEpiSoftmaxBwd) != 0;
         uint32_t chunk_phase = 0;
         uint32_t row_phase = 0;   // softmax: one phase of row_max / row_sum / row_read per tile
         bool ok = true;
@@ -1076,6 +1078,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float v[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
+                    store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
+                }
+            } else if (softmax_bwd) {
+                // Softmax backward fused into dP = dO V^T (N <= BN, one n-tile):
+                // dS = P * (dP - rowsum(P * dP)), the derivative SoftOp::_backward
+                // applies (tensor_ops.cpp:2056-2059), P read from p.aux (laid out
+                // like C). The two column halves of a row meet like the forward
+                // softmax's: each posts its partial row sum in its staging block.
+                float* xch = stage_w;
+                const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;
+                const float* prow = p.aux + coff + (int64_t)(rok ? gm : 0) * p.ldc;
+                auto rows_meet = [&](uint64_t* bar) {
+                    mbar_arrive(smem_u32(bar));
+                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueMaster);
+                    return __all_sync(0xffffffffu, met);
+                };
+                float sum = 0.f;
+                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_row + c, r);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (rok && c + j < p.N) sum += __ldg(prow + c + j) * (p.alpha * __uint_as_float(r[j]));
+                }
+                xch[lane] = sum;
+                if (!rows_meet(&ss->row_max)) { ok = false; break; }
+                sum = half ? pxch[lane] + sum : sum + pxch[lane];   // first half's columns first
+                if (!rows_meet(&ss->row_read)) { ok = false; break; }
+                row_phase ^= 1u;
+                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(t_row + c, r);
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float pv = (rok && c + j < p.N) ? __ldg(prow + c + j) : 0.f;
+                        v[j] = pv * (p.alpha * __uint_as_float(r[j]) - sum);
+                    }
                     store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
                 }
             } else {

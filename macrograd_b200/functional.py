@@ -10,6 +10,10 @@ arithmetic on the product path):
       macrograd/source/tensor_ops.cpp:4504-4517, 4723-4737
   attention_scores(...)                         matmul(Q/sqrt(d), K, mask, false, true)
       followed by softmax(-1), mini_shakespeare/include/transformer.h:233-234
+  matmul_view(...)                              the same product on strided views (the
+      attention head split/merge read and written in place)
+  attention_softmax_backward(...)               dP = dO V^T and the softmax derivative
+      (tensor_ops.cpp:2056-2059) in one kernel
 
 Shape rules, error conditions and messages follow the reference; the GEMM
 itself always runs in libmg_gemm.so (mg_matmul / mg_matmul_bias / mg_gemm).
@@ -148,6 +152,116 @@ def attention_scores(q: torch.Tensor, k: torch.Tensor, scale: float, causal: boo
                                 i32_array(a), i32_array(b), i32_array(bs) if bs else None,
                                 len(oshape), 0, 1, ctypes.c_float(scale), int(causal),
                                 _stream_handle(q, stream)))
+    return out
+
+
+def attention_softmax_backward(dO: torch.Tensor, v: torch.Tensor, p: torch.Tensor, alpha: float = 1.0,
+                               stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """dS = P * (G - rowsum(P * G)) with G = alpha * dO @ v^T, one kernel: the
+    attention backward's dP = dO V^T (the GEMM MatMulOp::_backward issues for
+    O = P V, tensor_ops.cpp:4504-4517) and the softmax derivative
+    SoftOp::_backward applies to it (tensor_ops.cpp:2056-2059), which the
+    reference runs as separate passes over the [.., L, L] scores."""
+    lib = _lib.load()
+    _check_operand(dO, "dO")
+    _check_operand(v, "v")
+    _check_operand(p, "p")
+    a, b, oshape, _, _ = equalize(dO.shape, v.shape, False, True)
+    if list(p.shape) != oshape:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"p must have the product's shape {oshape}")
+    out = torch.empty(oshape, device=dO.device, dtype=torch.float32)
+    check(lib.mg_matmul_softmax_backward(_ptr(out), _ptr(dO), _ptr(v), _ptr(p), i32_array(oshape), i32_array(a),
+                                         i32_array(b), len(oshape), 0, 1, ctypes.c_float(alpha),
+                                         _stream_handle(dO, stream)))
+    return out
+
+
+# ------------------------------------------------------------------ strided views
+def _view_operand(t: torch.Tensor, name: str):
+    """(trans, ld, batch strides) of a view whose logical last two dims are
+    [rows, cols] with one of the two at unit stride: trans = 0 when the
+    columns are contiguous (ld = row stride), 1 when the rows are (ld =
+    column stride, i.e. stored transposed)."""
+    if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must be a float32 CUDA tensor")
+    if t.dim() < 2:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must have at least 2 dims")
+    r, c = t.shape[-2], t.shape[-1]
+    sr, sc = t.stride(-2), t.stride(-1)
+    if sc == 1 or c == 1:
+        return 0, max(sr, c, 1), list(t.stride()[:-2])
+    if sr == 1 or r == 1:
+        return 1, max(sc, r, 1), list(t.stride()[:-2])
+    raise MacrogradError(_lib.MG_ERR_UNSUPPORTED,
+                         f"{name}: one of the last two dims must have unit stride (strides {tuple(t.stride())})")
+
+
+def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,
+                bias: Optional[torch.Tensor] = None, alpha: float = 1.0,
+                stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """out[..., M, N] = alpha * a[..., M, K] @ b[..., K, N] (+ bias) on strided
+    views, read and written in place -- no transposed or head-split copy.
+
+    For the multi-head attention of mini_shakespeare/include/transformer.h
+    (226-228, 244), which materialises `Q.view(B, L, H, d).transpose(1, 2)`
+    and its inverse with Tensor::transpose copies (tensor_ops.cpp:469-576):
+    here the head split is just strides of the GEMM operands and output
+    (row pitch E, batch strides L*E and d). Leading dims broadcast as in
+    Functional::matmul (size 1 or stride 0); one of each operand's last two
+    dims must have unit stride. Operands whose strides TMA cannot read
+    (not multiples of 16 bytes) are re-laid out by the library first."""
+    lib = _lib.load()
+    ta, lda, sa = _view_operand(a, "a")
+    tb, ldb, sb = _view_operand(b, "b")
+    M, K = a.shape[-2], a.shape[-1]
+    if b.shape[-2] != K:
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             f"Incompatible dimensions found inside a matmul() call.\n"
+                             f"Matrix0 shape: {tuple(a.shape)} | Matrix1 shape: {tuple(b.shape)}")
+    N = b.shape[-1]
+    nb = max(a.dim(), b.dim()) - 2
+    ash = [1] * (nb - (a.dim() - 2)) + list(a.shape[:-2])
+    bsh = [1] * (nb - (b.dim() - 2)) + list(b.shape[:-2])
+    sa = [0] * (nb - len(sa)) + sa
+    sb = [0] * (nb - len(sb)) + sb
+    batch = []
+    for i in range(nb):
+        if not (ash[i] == bsh[i] or ash[i] == 1 or bsh[i] == 1):
+            raise MacrogradError(_lib.MG_ERR_INVALID,
+                                 "Trying to matrix multiply two tensors with incompatible shapes.\n"
+                                 f"Found shapes | Matrix0: {tuple(a.shape)} | Matrix1: {tuple(b.shape)}")
+        batch.append(max(ash[i], bsh[i]))
+    if nb > _lib.MG_MAX_BATCH_DIMS:
+        raise MacrogradError(_lib.MG_ERR_UNSUPPORTED, f"more than {_lib.MG_MAX_BATCH_DIMS} leading dims")
+    oshape = batch + [M, N]
+    if out is None:
+        out = torch.empty(oshape, device=a.device, dtype=torch.float32)
+    if list(out.shape) != oshape or out.stride(-1) != 1:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"out must have shape {oshape} and unit column stride")
+    d = _lib.GemmDesc()
+    lib.mg_gemm_desc_init(ctypes.byref(d), M, N, K, ta, tb)
+    d.lda, d.ldb, d.ldc = lda, ldb, max(out.stride(-2), N)
+    d.batch_rank = nb
+    for i in range(nb):
+        d.batch[i] = batch[i]
+        d.a_batch_stride[i] = 0 if ash[i] == 1 else sa[i]
+        d.b_batch_stride[i] = 0 if bsh[i] == 1 else sb[i]
+        d.c_batch_stride[i] = out.stride(i)
+    d.alpha = alpha
+    if bias is not None:
+        _check_operand(bias, "bias")
+        bs = equalize_bias(bias.shape, oshape)
+        d.epilogue = _lib.MG_EPI_BIAS
+        # contiguous bias broadcast to out: element strides, 0 where broadcast
+        strides = [0] * len(bs)
+        acc = 1
+        for i in range(len(bs) - 1, -1, -1):
+            strides[i] = 0 if bs[i] == 1 else acc
+            acc *= bs[i]
+        d.bias_rs, d.bias_cs = strides[-2], strides[-1]
+        for i in range(nb):
+            d.bias_batch_stride[i] = strides[i]
+    check(lib.mg_gemm(ctypes.byref(d), _ptr(out), _ptr(a), _ptr(b), _ptr(bias), _stream_handle(a, stream)))
     return out
 
 

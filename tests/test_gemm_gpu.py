@@ -269,6 +269,53 @@ def test_k_split_of_the_last_wave(monkeypatch, pair, mode, sa, sb, ta, tb, bias_
     assert not np.array_equal(split, unsplit)
 
 
+@pytest.mark.parametrize("mode", MODES)
+def test_attention_head_split_as_strided_views(mode):
+    """The multi-head attention's head split / merge (transformer.h:226-228,
+    244) as strides of the GEMM operands and output: Q, K, V stay [B, L, E]
+    tensors, the [B, H, L, d] heads are views, and O is written straight into
+    its merged [B, L, E] layout -- against the oracle on materialised heads."""
+    set_mode(mode)
+    B_, L, H, d = 3, 96, 6, 64
+    E = H * d
+    q = ob.seeded_normal((B_, L, E), 861, 0.0, 0.125)
+    k = ob.seeded_normal((B_, L, E), 862, 0.0, 0.125)
+    v = ob.seeded_normal((B_, L, E), 863)
+    heads = lambda x: x.view(B_, L, H, d).transpose(1, 2)     # [B, H, L, d], no copy
+    qg, kg, vg = cuda(q), cuda(k), cuda(v)
+    S = F.matmul_view(heads(qg), heads(kg).transpose(-1, -2), alpha=0.125)
+    O = torch.empty(B_, L, E, device="cuda")
+    F.matmul_view(S, heads(vg), out=heads(O))
+    qh = np.ascontiguousarray(q.reshape(B_, L, H, d).transpose(0, 2, 1, 3))
+    kh = np.ascontiguousarray(k.reshape(B_, L, H, d).transpose(0, 2, 1, 3))
+    vh = np.ascontiguousarray(v.reshape(B_, L, H, d).transpose(0, 2, 1, 3))
+    S_ref = ob.oracle_matmul(qh * np.float32(0.125), kh, False, True)
+    assert_close(host(S), S_ref, mode, "scores on head views")
+    O_ref = ob.oracle_matmul(host(S), vh).transpose(0, 2, 1, 3).reshape(B_, L, E)
+    assert_close(host(O), O_ref, mode, "output merged in place")
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("shape", [(4, 6, 256, 64), (3, 2, 200, 64), (2, 96, 40)])
+def test_fused_softmax_backward(mode, shape):
+    """dS = P * (dP - rowsum(P * dP)), dP = dO V^T, from one launch, against
+    the same expression in float64 from the oracle's GEMM inputs (the
+    reference's SoftOp::_backward, tensor_ops.cpp:2056-2059)."""
+    set_mode(mode)
+    L = shape[-2]
+    q = ob.seeded_normal(shape, 871, 0.0, 0.125)
+    k = ob.seeded_normal(shape, 872, 0.0, 0.125)
+    v = ob.seeded_normal(shape, 873)
+    dO = ob.seeded_normal(shape, 874)
+    P = host(F.attention_scores(cuda(q), cuda(k), 0.125, causal=True))
+    dS = host(F.attention_softmax_backward(cuda(dO), cuda(v), cuda(P)))
+    dP = np.matmul(dO.astype(np.float64), np.swapaxes(v.astype(np.float64), -1, -2))
+    P64 = P.astype(np.float64)
+    ref = P64 * (dP - (P64 * dP).sum(-1, keepdims=True))
+    assert dS.shape == ref.shape == P.shape[:-1] + (L,)
+    assert_close(dS, ref.astype(np.float32), mode, "softmax backward")
+
+
 def test_k_split_with_accumulate(monkeypatch):
     """beta = 1 (gradient accumulation) is applied once, by the final range."""
     monkeypatch.setenv("MG_GEMM_SPLIT_MIN_KB", "1")
