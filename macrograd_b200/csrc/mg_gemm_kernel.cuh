@@ -1,9 +1,9 @@
 // mg_gemm_kernel.cuh -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
-// Computes C = alpha * op(A) op(B) (+ bias) (+ beta * C), or a fused row
-// softmax of it, on fp32 operands through the TF32 tensor cores: one product
-// per term (TF32 mode), or the 3xTF32 split hi*hi + hi*lo + lo*hi
-// (fp32-accurate mode).
+// Computes C = alpha * op(A) op(B) (+ bias) (+ beta * C), a fused row softmax
+// of it, or the fused softmax backward P * (G - rowsum(P * G)) of it, on fp32
+// operands through the TF32 tensor cores: one product per term (TF32 mode), or
+// the 3xTF32 split hi*hi + hi*lo + lo*hi (fp32-accurate mode).
 //
 // Two variants of one template:
 //   kPair = false  one CTA per SM, output tile 128 x BN, MMA M=128
@@ -28,8 +28,9 @@
 // Roles (512 threads = 16 warps per CTA, one CTA per SM):
 //   warps 0-7   epilogue: warp w owns TMEM lanes 32(w%4).. (tile rows) and the
 //               column half w/4. Per chunk: master (+)= partial. Per tile:
-//               alpha / bias / beta / store from the master; the row softmax
-//               runs in warps 0-3 with one thread per full row.
+//               alpha / bias / beta / store from the master; for the row
+//               softmax (and its backward) warps w and w^4 reduce their halves
+//               of each row and meet through shared memory.
 //   warps 8-11  split (3xTF32): lo tile of every landed stage; in both modes
 //               they report the landed stage to the MMA issuer.
 //   warp 12     TMA producer (one lane), into this CTA's shared memory.
@@ -37,7 +38,13 @@
 //   warps 14-15 export (fused all-gather): once the epilogue has written a tile
 //               into this GPU's C, copy its rows into every peer's C over
 //               NVLink, so the epilogue never waits on the fabric.
-// TMEM: columns [0, BN) partial, [BN, 2BN) master.
+// TMEM: columns [0, BN) partial, [BN, 2BN) master; when every tile is a
+// single chunk (p.dbuf) the two regions are alternate accumulators instead,
+// so one tile's MMAs run during the previous tile's epilogue.
+//
+// Work units: whole tiles, dealt round-robin; the last partial wave may be
+// split over K into ranges whose fp32 partials the tile's final range adds
+// (unit_at, GemmParams::nlev), the grid then launched cooperatively.
 //
 // Operand layouts in shared memory (per stage, 1024-byte aligned):
 //   K-major tile (op(X) rows contiguous in K): R rows x 128 B, one TMA box
@@ -92,8 +99,8 @@ enum : int {
     kWaitMmaPartialFree = 3,
     kWaitMmaStage = 4,
     kWaitEpiloguePartial = 5,
-    kWaitEpilogueMaster = 6,
-    kWaitEpilogueMasterFree = 7,
+    // 6: no longer used
+    kWaitEpilogueRows = 7,
     kWaitExportTile = 8,
     kWaitPartials = 9
 };
@@ -1037,7 +1044,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // every epilogue thread of the CTA has arrived on `bar` this tile
                 auto rows_meet = [&](uint64_t* bar) {
                     mbar_arrive(smem_u32(bar));
-                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueMaster);
+                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueRows);
                     return __all_sync(0xffffffffu, met);
                 };
                 float mx = -INFINITY;
@@ -1091,7 +1098,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float* prow = p.aux + coff + (int64_t)(rok ? gm : 0) * p.ldc;
                 auto rows_meet = [&](uint64_t* bar) {
                     mbar_arrive(smem_u32(bar));
-                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueMaster);
+                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueRows);
                     return __all_sync(0xffffffffu, met);
                 };
                 float sum = 0.f;

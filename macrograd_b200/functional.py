@@ -1,7 +1,10 @@
 """Host-side mirror of Macrograd's matmul API over the sm_100a library.
 
-Mirrors, for torch CUDA tensors (device memory and streams only; no torch
-arithmetic on the product path):
+Mirrors, for torch CUDA tensors (torch provides device memory and streams;
+every GEMM runs in libmg_gemm.so -- torch arithmetic appears only in
+matmul_backward's non-GEMM steps: the bias gradient sum(dC) and the `+=`
+reduction of a broadcast operand's gradient when its batch cannot fold into
+K, the reference's own separate passes there, tensor_ops.cpp:3345-3451):
   matmul(mat0, mat1, transA, transB)            Functional::matmul
       macrograd/source/tensor_ops.cpp:4482-4694
   matmul(mat0, mat1, bias, transA, transB)      Functional::matmul with bias
