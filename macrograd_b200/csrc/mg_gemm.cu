@@ -436,60 +436,12 @@ mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace&
 
 int tuning_int(const char* name, int dflt, int lo, int hi);
 
-// Plans the split of the last, partial wave of tiles over the K dimension
-// (GemmParams::nlev): with `units` CTAs (pairs) resident, whole tiles fill
-// floor(T / units) waves; the R remaining tiles are cut into K-ranges so that
-// every unit gets work -- all R tiles at once in floor(units / R) ranges each
-// when that is >= 2, else level by level, 2, 4, 8... ranges per tile, as many
-// tiles per level as the units allow. Besides filling the idle units, the
-// levels finish their tiles at staggered times (the fused all-gather then
-// sends them while the later levels compute). Returns the workspace slots
-// needed (0: no split, every unit a whole tile).
+// K split of the last partial wave (mg_plan.h): MG_GEMM_SPLIT=0 turns it off,
+// MG_GEMM_SPLIT_MIN_KB sets the shortest range in K-blocks (default 16).
 int plan_split(mg::GemmParams& gp, int units)
 {
-    gp.full_tiles = gp.total_tiles;
-    gp.nlev = 0;
-    if (units < 2 || !tuning_int("MG_GEMM_SPLIT", 1, 0, 1)) return 0;
-    const int T = gp.total_tiles, KB = gp.num_kb;
-    const int waves = T / units, R = T - waves * units;
-    if (R == 0) return 0;
-    const int min_kb = tuning_int("MG_GEMM_SPLIT_MIN_KB", 16, 1, 1 << 20);   // K-blocks per range at least
-    int S[mg::kMaxLevels], Rl[mg::kMaxLevels], n = 0, rem = R;
-    double t = 0.0;
-    if (units / R >= 2) {
-        const int s = std::min(std::min(units / R, 8), KB / min_kb);
-        if (s >= 2) {
-            S[0] = s;
-            Rl[0] = R;
-            n = 1;
-            rem = 0;
-            t = 1.0 / s;
-        }
-    } else {
-        for (int s = 2; rem > 0 && n < mg::kMaxLevels && KB / s >= min_kb; s *= 2) {
-            const int r = std::min(rem, units / s);
-            if (r == 0) break;
-            S[n] = s;
-            Rl[n] = r;
-            ++n;
-            rem -= r;
-            t += 1.0 / s;
-        }
-    }
-    if (rem > 0 || n == 0) return 0;
-    if (waves + t > 0.95 * (waves + 1)) return 0;   // not worth the partial sums
-    gp.full_tiles = waves * units;
-    int tile0 = gp.full_tiles, slot0 = 0;
-    for (int l = 0; l < n; ++l) {
-        gp.lev_split[l] = S[l];
-        gp.lev_tiles[l] = Rl[l];
-        gp.lev_tile0[l] = tile0;
-        gp.lev_slot0[l] = slot0;
-        tile0 += Rl[l];
-        slot0 += Rl[l] * (S[l] - 1);
-    }
-    gp.nlev = n;
-    return slot0;
+    const int min_kb = tuning_int("MG_GEMM_SPLIT", 1, 0, 1) ? tuning_int("MG_GEMM_SPLIT_MIN_KB", 16, 1, 1 << 20) : 0;
+    return mg::plan_k_split(gp.plan, gp.total_tiles, units, gp.num_kb, min_kb);
 }
 
 // Plans the K split for `units` resident CTAs (pairs) and takes its workspace:
@@ -501,19 +453,19 @@ bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, 
     const int nslots = allow ? plan_split(gp, units) : 0;
     gp.tail_share = 0;
     if (nslots == 0) {
-        gp.full_tiles = gp.total_tiles;
-        gp.nlev = 0;
+        gp.plan.full_tiles = gp.total_tiles;
+        gp.plan.nlev = 0;
         return false;
     }
     const size_t part = (size_t)nslots * 2 * mg::kBM * BN * sizeof(float);
     // fused all-gather: a counter per last-level tile half, for the shared export
     const bool tail = gp.export_peers && gp.npeers > 0 && tuning_int("MG_GEMM_TAIL_SHARE", 1, 0, 1);
-    const size_t nflags = (size_t)nslots * 2 + (tail ? (size_t)gp.lev_tiles[gp.nlev - 1] * 2 : 0);
+    const size_t nflags = (size_t)nslots * 2 + (tail ? (size_t)gp.plan.lev_tiles[gp.plan.nlev - 1] * 2 : 0);
     const size_t flags = nflags * sizeof(unsigned int);
     uint8_t* w = static_cast<uint8_t*>(ws ? ws->get(part + flags) : nullptr);
     if (!w || cudaMemsetAsync(w + part, 0, flags, st) != cudaSuccess) {
-        gp.full_tiles = gp.total_tiles;
-        gp.nlev = 0;
+        gp.plan.full_tiles = gp.total_tiles;
+        gp.plan.nlev = 0;
         return false;
     }
     gp.part_ws = reinterpret_cast<float*>(w);
@@ -581,8 +533,8 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
                 return MG_OK;
             }
             (void)cudaGetLastError();   // not launchable cooperatively here: run unsplit
-            gp.full_tiles = gp.total_tiles;
-            gp.nlev = 0;
+            gp.plan.full_tiles = gp.total_tiles;
+            gp.plan.nlev = 0;
             gp.tail_share = 0;
             gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
             cfg.attrs = attr;
@@ -610,8 +562,8 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
                 return MG_OK;
             }
             (void)cudaGetLastError();
-            gp.full_tiles = gp.total_tiles;
-            gp.nlev = 0;
+            gp.plan.full_tiles = gp.total_tiles;
+            gp.plan.nlev = 0;
             gp.tail_share = 0;
             gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
         }
@@ -889,7 +841,8 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const int64_t total = nbatch * gp.tiles_per_batch;
     if (total >= (1ll << 31)) return fail(MG_ERR_UNSUPPORTED, "too many output tiles (%lld)", (long long)total);
     gp.total_tiles = (int)total;
-    gp.full_tiles = gp.total_tiles;   // no K split unless launch_tc plans one
+    gp.plan.full_tiles = gp.total_tiles;   // no K split unless launch_tc plans one
+    gp.plan.num_kb = gp.num_kb;
     gp.group_m = 16;
     gp.chunk_kb = tuning_int("MG_GEMM_CHUNK_KB", mg::kChunkKb, 1, 64);
     gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);

@@ -66,6 +66,7 @@
 
 #include <stdint.h>
 
+#include "mg_plan.h"
 #include "mg_ptx.cuh"
 
 namespace mg {
@@ -85,7 +86,6 @@ constexpr int kExportThreads = 64;
 constexpr int kThreads = 16 * 32;
 constexpr int kMaxBatchDims = 6;
 constexpr int kMaxPeers = 8;
-constexpr int kMaxLevels = 4;       // split levels of the last partial wave
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
 constexpr uint32_t kSleepHintNs = 20000u;          // try_wait suspend hint
@@ -147,16 +147,9 @@ struct GemmParams {
     int export_peers;
     int export_vec;             // N, ldc and every destination allow 16-byte copies
     float* peers[kMaxPeers];
-    // Work units. Whole tiles [0, full_tiles) are dealt round-robin to the
-    // CTAs (pairs). The rest -- the last, partial wave -- is split over the
-    // K dimension in up to kMaxLevels levels: level l takes lev_tiles[l] tiles
-    // from lev_tile0[l], cuts each into lev_split[l] K-ranges and gives one
-    // range to each of CTAs (pairs) 0 .. lev_tiles[l] * lev_split[l] - 1. The
-    // last range of a tile adds the other ranges' fp32 partials (workspace
-    // slots from lev_slot0[l]) into its output, in range order.
-    int full_tiles;
-    int nlev;
-    int lev_split[kMaxLevels], lev_tiles[kMaxLevels], lev_tile0[kMaxLevels], lev_slot0[kMaxLevels];
+    // Work units: whole tiles, then the K-split levels of the last partial
+    // wave (mg_plan.h; units = CTAs, or CTA pairs).
+    UnitPlan plan;
     float* part_ws;             // [slot][cta rank][BN/32 chunks][128 rows][32] floats
     unsigned int* part_flag;    // [slot][cta rank]: epilogue warps that stored their part
     // Fused all-gather with split levels: the last level's tiles finish last,
@@ -178,43 +171,11 @@ struct TileCoord {
     int batch, mt, nt;
 };
 
-// One work unit: K-blocks [kb0, kb1) of a tile; kind 0 = the whole tile,
-// 1 = a partial range (stores its fp32 sum in workspace slot `slot`),
-// 2 = the final range (adds slots slot .. slot + nsib - 1 and writes C).
-struct Unit {
-    int tile, kb0, kb1, kind, slot, nsib;
-};
-
 // The i-th unit of CTA (pair) u0 of ustep; false past the last one. Every role
 // of the CTA walks the same list.
 __device__ __forceinline__ bool unit_at(const GemmParams& p, int u0, int ustep, int i, Unit& u)
 {
-    const int nw = p.full_tiles > u0 ? (p.full_tiles - u0 + ustep - 1) / ustep : 0;
-    if (i < nw) {
-        u.tile = u0 + i * ustep;
-        u.kb0 = 0;
-        u.kb1 = p.num_kb;
-        u.kind = 0;
-        u.slot = 0;
-        u.nsib = 0;
-        return true;
-    }
-    int j = i - nw;
-    for (int l = 0; l < p.nlev; ++l) {
-        const int S = p.lev_split[l];
-        if (u0 >= p.lev_tiles[l] * S) continue;
-        if (j-- > 0) continue;
-        const int tl = u0 / S, part = u0 - tl * S;
-        u.tile = p.lev_tile0[l] + tl;
-        u.kb0 = (int)((int64_t)p.num_kb * part / S);
-        u.kb1 = (int)((int64_t)p.num_kb * (part + 1) / S);
-        const int base = p.lev_slot0[l] + tl * (S - 1);
-        u.kind = part == S - 1 ? 2 : 1;
-        u.slot = part == S - 1 ? base : base + part;
-        u.nsib = part == S - 1 ? S - 1 : 0;
-        return true;
-    }
-    return false;
+    return plan_unit_at(p.plan, u0, ustep, i, u);
 }
 
 __device__ __forceinline__ TileCoord decode_tile(int t, const GemmParams& p)
@@ -805,7 +766,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!wait_count(&ss->tiles_stored, (unsigned int)kEpiWarps * (j + 1u), ss, p, kWaitExportTile))
                     break;
                 if (u.kind == 1) continue;   // a partial K-range: its tile leaves with the final range
-                if (p.tail_share && u.tile >= p.lev_tile0[p.nlev - 1]) continue;   // shared below
+                if (p.tail_share && u.tile >= p.plan.lev_tile0[p.plan.nlev - 1]) continue;   // shared below
                 __threadfence();
                 const TileCoord tc = decode_tile(u.tile, p);
                 int idx[kMaxBatchDims];
@@ -826,8 +787,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (p.tail_share) {
                 // this CTA's share of the last level's rows (every CTA of the grid)
                 constexpr int kHalves = kPair ? 2 : 1;
-                const int t0 = p.lev_tile0[p.nlev - 1];
-                const int R = p.lev_tiles[p.nlev - 1] * kHalves * kBM;
+                const int t0 = p.plan.lev_tile0[p.plan.nlev - 1];
+                const int R = p.plan.lev_tiles[p.plan.nlev - 1] * kHalves * kBM;
                 const int G = (int)gridDim.x, b = (int)blockIdx.x;
                 const int r_end = (int)((int64_t)R * (b + 1) / G);
                 for (int r = (int)((int64_t)R * b / G); r < r_end;) {
@@ -1149,11 +1110,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             tc_fence_before();
-            if (p.tail_share && u.kind == 2 && u.tile >= p.lev_tile0[p.nlev - 1]) {
+            if (p.tail_share && u.kind == 2 && u.tile >= p.plan.lev_tile0[p.plan.nlev - 1]) {
                 // a last-level tile half is in C: any CTA's export warps may send it
                 __threadfence();
                 __syncwarp();
-                if (lane == 0) atomicAdd(&p.tail_flag[(u.tile - p.lev_tile0[p.nlev - 1]) * (kPair ? 2 : 1) + (int)rank], 1u);
+                if (lane == 0) atomicAdd(&p.tail_flag[(u.tile - p.plan.lev_tile0[p.plan.nlev - 1]) * (kPair ? 2 : 1) + (int)rank], 1u);
             }
             if (p.dbuf) {
                 // done with this accumulator: the MMAs of the tile after next may use it

@@ -1,0 +1,103 @@
+// plan_check.cpp -- CPU check of the GEMM kernel's work-unit plan
+// (macrograd_b200/csrc/mg_plan.h, the same code the kernel and the launcher
+// use). Built and run by tests/test_plan.py; prints "ok" or the first failure.
+#include <cstdio>
+#include <map>
+#include <vector>
+
+#include "mg_plan.h"
+
+using mg::Unit;
+using mg::UnitPlan;
+
+static int fail(const char* what, int T, int U, int KB, int mk)
+{
+    std::printf("FAIL %s (tiles %d, units %d, num_kb %d, min_kb %d)\n", what, T, U, KB, mk);
+    return 1;
+}
+
+// Every (tile, K-block) is covered exactly once; partial slots are written by
+// exactly one range of their tile and read by that tile's final range; a
+// split never makes any unit's work longer than whole-tile waves would.
+static int check(int T, int U, int KB, int mk, int* nsplit)
+{
+    UnitPlan w;
+    const int nslots = mg::plan_k_split(w, T, U, KB, mk);
+    if (w.nlev > 0) ++*nsplit;
+    if ((nslots > 0) != (w.nlev > 0)) return fail("slot count vs levels", T, U, KB, mk);
+    const int grid = w.nlev > 0 ? U : (T < U ? T : U);
+    std::vector<int> cover((size_t)T * KB, 0);
+    std::map<int, int> slot_writer;            // slot -> tile
+    std::map<int, std::pair<int, int>> finals; // tile -> (first slot, count)
+    int worst = 0;
+    for (int u0 = 0; u0 < grid; ++u0) {
+        Unit u;
+        int work = 0;
+        for (int i = 0; mg::plan_unit_at(w, u0, grid, i, u); ++i) {
+            if (u.tile < 0 || u.tile >= T || u.kb0 < 0 || u.kb1 > KB || u.kb0 >= u.kb1)
+                return fail("unit out of range", T, U, KB, mk);
+            for (int kb = u.kb0; kb < u.kb1; ++kb) cover[(size_t)u.tile * KB + kb]++;
+            work += u.kb1 - u.kb0;
+            if (u.kind == 1) {
+                if (slot_writer.count(u.slot)) return fail("slot written twice", T, U, KB, mk);
+                slot_writer[u.slot] = u.tile;
+            } else if (u.kind == 2) {
+                if (u.kb1 != KB) return fail("final range does not end the tile", T, U, KB, mk);
+                finals[u.tile] = {u.slot, u.nsib};
+            } else if (u.kb0 != 0 || u.kb1 != KB) {
+                return fail("whole tile with a partial range", T, U, KB, mk);
+            }
+        }
+        worst = work > worst ? work : worst;
+    }
+    for (size_t i = 0; i < cover.size(); ++i)
+        if (cover[i] != 1) return fail("K-block not covered exactly once", T, U, KB, mk);
+    int read = 0;
+    for (auto& f : finals) {
+        for (int q = 0; q < f.second.second; ++q) {
+            auto it = slot_writer.find(f.second.first + q);
+            if (it == slot_writer.end() || it->second != f.first) return fail("final reads a foreign slot", T, U, KB, mk);
+        }
+        read += f.second.second;
+    }
+    if (read != (int)slot_writer.size() || (int)slot_writer.size() != nslots)
+        return fail("slots written / read / planned disagree", T, U, KB, mk);
+    const int whole = ((T + grid - 1) / grid) * KB;   // K-blocks of the busiest unit without a split
+    if (w.nlev > 0 && worst > whole) return fail("split made the busiest unit slower", T, U, KB, mk);
+    return 0;
+}
+
+static int expect(int T, int U, int KB, int mk, int nlev, const int* split, const int* tiles)
+{
+    UnitPlan w;
+    mg::plan_k_split(w, T, U, KB, mk);
+    if (w.nlev != nlev) return fail("unexpected level count", T, U, KB, mk);
+    for (int l = 0; l < nlev; ++l)
+        if (w.lev_split[l] != split[l] || w.lev_tiles[l] != tiles[l]) return fail("unexpected level", T, U, KB, mk);
+    return 0;
+}
+
+int main()
+{
+    int nsplit = 0;
+    const int units[] = {1, 2, 3, 37, 74, 148};
+    const int kbs[] = {1, 8, 12, 32, 256};
+    const int mks[] = {1, 16};
+    for (int T = 1; T < 320; ++T)
+        for (int U : units)
+            for (int KB : kbs)
+                for (int mk : mks)
+                    if (check(T, U, KB, mk, &nsplit)) return 1;
+    for (int T : {512, 1024, 1184, 2048})
+        for (int U : units)
+            if (check(T, U, 256, 16, &nsplit)) return 1;
+    // the row-sharded 8192^3 shapes on 74 SM pairs
+    const int s8[] = {2, 4}, t8[] = {37, 17};
+    const int s4[] = {2}, t4[] = {34};
+    if (expect(128, 74, 256, 16, 2, s8, t8)) return 1;    // 8 GPUs: 1 wave + halves + quarters
+    if (expect(256, 74, 256, 16, 1, s4, t4)) return 1;    // 4 GPUs: 3 waves + halves
+    if (expect(1024, 74, 256, 16, 0, nullptr, nullptr)) return 1;   // 1 GPU: saves < 5 %
+    if (nsplit == 0) return fail("no case split at all", 0, 0, 0, 0);
+    std::printf("ok %d split plans checked\n", nsplit);
+    return 0;
+}
