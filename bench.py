@@ -310,31 +310,66 @@ def main():
     value = flops / (ms_per_step * 1e-3) / 1e12
 
     # ---- end to end through the public API from pinned host memory
+    # Every step copies its A rows in from pinned host memory, runs the GEMM
+    # (and the all-gather) and copies its C rows back out; consecutive steps
+    # are pipelined on three streams with double buffers (copy-in of step i+1
+    # and copy-out of step i-1 run while step i computes), the way a stream of
+    # GEMMs on host data would be driven.
     e2e = None
     if not args.no_e2e:
         A_h = A.cpu().pin_memory()
         C_h = torch.empty(rows, n, dtype=torch.float32).pin_memory()
-        A_d = torch.empty_like(A)
+        A_d = [torch.empty_like(A) for _ in range(2)]
+        if fused:
+            C_e = [C_full] + [torch.empty(n, n, device=dev)]
+            peers_e = [peers, PeerRows(C_e[1])]
+        elif world > 1:
+            C_e = [C_full, torch.empty(n, n, device=dev)]
+        else:
+            C_e = [C_local, torch.empty(rows, n, device=dev)]
+        s_in = torch.cuda.Stream(dev)
+        s_out = torch.cuda.Stream(dev)
+        ev = {k: [torch.cuda.Event() for _ in range(2)] for k in ("in", "comp", "out")}
+        used = [False, False]
 
-        def e2e_step():
-            A_d.copy_(A_h, non_blocking=True)
+        def e2e_step(i):
+            b = i % 2
+            if used[b]:
+                s_in.wait_event(ev["comp"][b])          # the GEMM that read A_d[b] is done
+            with torch.cuda.stream(s_in):
+                A_d[b].copy_(A_h, non_blocking=True)
+                ev["in"][b].record(s_in)
+            stream.wait_event(ev["in"][b])
+            if used[b]:
+                stream.wait_event(ev["out"][b])         # C[b]'s previous rows are on the host
             if fused:
-                scatter_matmul(A_d, B, peers, r0)
+                scatter_matmul(A_d[b], B, peers_e[b], r0)
                 dist.all_reduce(fence)
-                C_h.copy_(C_full[r0:r1], non_blocking=True)
+                src = C_e[b][r0:r1]
+            elif world > 1:
+                sharded_matmul(A_d[b], B, full_out=C_e[b], local_out=C_local)
+                src = C_e[b][r0:r1]
             else:
-                sharded_matmul(A_d, B, full_out=C_full if world > 1 else None, local_out=C_local)
-                C_h.copy_(C_local, non_blocking=True)
+                sharded_matmul(A_d[b], B, local_out=C_e[b])
+                src = C_e[b]
+            ev["comp"][b].record(stream)
+            s_out.wait_event(ev["comp"][b])
+            with torch.cuda.stream(s_out):
+                C_h.copy_(src, non_blocking=True)
+                ev["out"][b].record(s_out)
+            used[b] = True
 
-        for _ in range(2):
-            e2e_step()
+        for i in range(2):
+            e2e_step(i)
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for _ in range(args.steps):
-            e2e_step()
+        s_in.wait_event(e0)
+        for i in range(args.steps):
+            e2e_step(i)
+        stream.wait_stream(s_out)
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
@@ -346,8 +381,12 @@ def main():
                "h2d_bytes_per_step": int(A_h.numel() * 4 * world),
                "d2h_bytes_per_step": int(C_h.numel() * 4 * world),
                "ms_per_step": e_ms,
-               "note": "per step: A row shard host->device (pinned), GEMM, all-gather, "
-                       "own C rows device->host; B resident like weights"}
+               "note": "per step: A row shard host->device (pinned), GEMM, all-gather, own C rows "
+                       "device->host; B resident like weights; steps pipelined on three streams "
+                       "(double-buffered A and C)"}
+        if fused:
+            dist.barrier(device_ids=[local_rank])
+            peers_e[1].close()
 
     if world > 1:
         dist.barrier(device_ids=[local_rank])             # no rank still writes into a peer's C
