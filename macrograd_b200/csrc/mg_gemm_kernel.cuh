@@ -1030,8 +1030,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         sum += e;
                         r[j] = __float_as_uint(e);
                     }
-                    tmem_st32(t_row + c, r);
+                    tmem_st32_async(t_row + c, r);
                 }
+                tmem_wait_st();   // the exps are in TMEM before the scaling pass reads them
                 xch[32 + lane] = sum;
                 if (!rows_meet(&ss->row_sum)) { ok = false; break; }
                 // the row's sum: first half's columns, then the second half's
