@@ -34,9 +34,9 @@ METRIC = "fp32-accurate matmul TFLOP/s & % TF32 roofline at 1/2/4/8 B200 vs host
 UNIT = "TFLOP/s"
 WORKLOAD = "square fp32 GEMM 8192x8192x8192, rows of A sharded over the GPUs, C rows all-gathered"
 
-# DRAM bytes (read + write) of one 8192^3 launch of the GEMM kernel, from the
-# ncu capture summarised in profiles/dram_mg_gemm_tc_kernel_8192.md
-# (dram__bytes_read.sum + dram__bytes_write.sum; null where not captured).
+# DRAM bytes (read + write) of one 8192^3 launch of the GEMM kernel, measured
+# with ncu (dram__bytes_read.sum + dram__bytes_write.sum of the 3xTF32 launch;
+# null where not captured).
 NCU_TRAFFIC_BYTES_PER_LAUNCH = {"3xtf32": 2568310272 + 255417856, "tf32": None}
 
 
