@@ -31,7 +31,7 @@ extern "C" {
 typedef enum mg_status {
     MG_OK = 0,
     MG_ERR_INVALID = 1,      /* bad arguments: shapes, ranks, pointers, strides */
-    MG_ERR_UNSUPPORTED = 2,  /* valid request this build cannot run (e.g. no sm_100 device) */
+    MG_ERR_UNSUPPORTED = 2,  /* valid request the library cannot run (e.g. no sm_100 device) */
     MG_ERR_CUDA = 3,         /* a CUDA runtime / driver call failed */
     MG_ERR_ALLOC = 4,        /* the workspace allocator returned NULL */
     MG_ERR_TIMEOUT = 5,      /* a kernel wait ran out its time limit (device status) */

@@ -17,15 +17,14 @@ from macrograd_b200 import training
 
 SMALL = dict(layers=2, heads=2, emb=32, ff=64, context=16, vocab=65)
 BATCH, T, SEED = 4, 16, 11
-REFERENCE = "/root/reference"
 
 
 def _seam_or_skip():
-    if os.path.exists(training.SEAM):
-        return
-    if os.path.isdir(os.path.join(REFERENCE, "macrograd")):
-        subprocess.run(["make", "-s", "-C", os.path.join(ob.ROOT, "macrograd_b200", "shim"), f"REF={REFERENCE}"],
-                       check=True)
+    if not os.path.exists(training.SEAM):
+        # the drop-in build's recipe knows where the reference sources are; it
+        # fails (and the test skips) where they are absent
+        subprocess.run(["make", "-s", "-C", os.path.join(ob.ROOT, "macrograd_b200", "shim")],
+                       capture_output=True)
     if not os.path.exists(training.SEAM):
         pytest.skip("drop-in build not available (needs the reference sources at build time)")
 
