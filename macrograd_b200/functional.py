@@ -180,23 +180,27 @@ def attention_softmax_backward(dO: torch.Tensor, v: torch.Tensor, p: torch.Tenso
 
 
 # ------------------------------------------------------------------ strided views
-def _view_operand(t: torch.Tensor, name: str):
+def view_layout(shape: Sequence[int], strides: Sequence[int], name: str = "operand"):
     """(trans, ld, batch strides) of a view whose logical last two dims are
     [rows, cols] with one of the two at unit stride: trans = 0 when the
     columns are contiguous (ld = row stride), 1 when the rows are (ld =
     column stride, i.e. stored transposed)."""
+    if len(shape) < 2:
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must have at least 2 dims")
+    r, c = shape[-2], shape[-1]
+    sr, sc = strides[-2], strides[-1]
+    if sc == 1 or c == 1:
+        return 0, max(sr, c, 1), list(strides[:-2])
+    if sr == 1 or r == 1:
+        return 1, max(sc, r, 1), list(strides[:-2])
+    raise MacrogradError(_lib.MG_ERR_UNSUPPORTED,
+                         f"{name}: one of the last two dims must have unit stride (strides {tuple(strides)})")
+
+
+def _view_operand(t: torch.Tensor, name: str):
     if not isinstance(t, torch.Tensor) or not t.is_cuda or t.dtype != torch.float32:
         raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must be a float32 CUDA tensor")
-    if t.dim() < 2:
-        raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must have at least 2 dims")
-    r, c = t.shape[-2], t.shape[-1]
-    sr, sc = t.stride(-2), t.stride(-1)
-    if sc == 1 or c == 1:
-        return 0, max(sr, c, 1), list(t.stride()[:-2])
-    if sr == 1 or r == 1:
-        return 1, max(sc, r, 1), list(t.stride()[:-2])
-    raise MacrogradError(_lib.MG_ERR_UNSUPPORTED,
-                         f"{name}: one of the last two dims must have unit stride (strides {tuple(t.stride())})")
+    return view_layout(list(t.shape), list(t.stride()), name)
 
 
 def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None,

@@ -38,3 +38,22 @@ def test_fold_batch_for_broadcast_weight_gradient():
         ([2048, 384], [2048, 384])
     assert F._fold_batch([8, 256, 384], [8, 256, 384], [8, 384, 384], True, False) is None
     assert F._fold_batch([8, 384, 256], [8, 256, 384], [1, 384, 384], False, False) is None
+
+
+def test_view_layout_reads_strides_of_head_split_views():
+    """functional.matmul_view maps torch views onto the descriptor: which of the
+    last two dims is contiguous decides the transpose flag and the row pitch,
+    the leading strides become batch strides (no copy of the head split)."""
+    import torch
+
+    from macrograd_b200 import functional as F
+
+    B, L, H, d = 2, 5, 3, 4
+    E = H * d
+    heads = torch.zeros(B, L, E).view(B, L, H, d).transpose(1, 2)   # [B, H, L, d]
+    assert F.view_layout(heads.shape, heads.stride()) == (0, E, [L * E, d])
+    kt = heads.transpose(-1, -2)
+    assert F.view_layout(kt.shape, kt.stride()) == (1, E, [L * E, d])
+    bad = torch.zeros(4, 6, 8)[:, ::2, ::2]
+    with pytest.raises(F.MacrogradError):
+        F.view_layout(bad.shape, bad.stride())
