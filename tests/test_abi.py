@@ -116,3 +116,25 @@ def test_no_device_reports_cuda_error_not_abort():
     buf = (ctypes.c_float * 16)()
     rc = lib.mg_gemm(ctypes.byref(d), buf, buf, buf, None, None)
     assert rc in (_lib.MG_ERR_CUDA, _lib.MG_ERR_UNSUPPORTED)
+
+
+def test_softmax_backward_entry_errors_return_status():
+    """mg_matmul_softmax_backward: P is required, its epilogue cannot be
+    requested through mg_gemm (no P there), N <= 256, shapes as mg_matmul."""
+    lib = mg.load()
+    P = (ctypes.c_float * 16)()
+    o, a, b = i32_array([4, 4]), i32_array([4, 8]), i32_array([4, 8])
+    assert lib.mg_matmul_softmax_backward(None, None, None, None, o, a, b, 2, 0, 1, 1.0, None) == \
+        _lib.MG_ERR_INVALID
+    assert "P is NULL" in lib.mg_last_error().decode()
+    bad = i32_array([4, 5])
+    assert lib.mg_matmul_softmax_backward(None, None, None, P, bad, a, b, 2, 0, 1, 1.0, None) == \
+        _lib.MG_ERR_INVALID
+    d = _lib.GemmDesc()
+    lib.mg_gemm_desc_init(ctypes.byref(d), 4, 4, 8, 0, 1)
+    d.epilogue = 8                      # the internal softmax-backward flag
+    buf = (ctypes.c_float * 64)()
+    assert lib.mg_gemm(ctypes.byref(d), buf, buf, buf, None, None) == _lib.MG_ERR_INVALID
+    lib.mg_gemm_desc_init(ctypes.byref(d), 4, 300, 8, 0, 1)
+    d.epilogue = 8
+    assert lib.mg_gemm(ctypes.byref(d), buf, buf, buf, None, None) == _lib.MG_ERR_INVALID
