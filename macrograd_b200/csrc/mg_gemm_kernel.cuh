@@ -521,6 +521,59 @@ __device__ __noinline__ void add_partials(const float* slot0, int nsib, size_t s
     }
 }
 
+// Row softmax passes over one thread's TMEM row, columns [c0, c1) in blocks
+// of 32. Column n's logit is alpha * acc[n] + brow[n * bcs] (brow null: no
+// bias); columns n >= lim (past N, or past the causal diagonal) are -inf and
+// their bias is never read. Out of line like the partial helpers: inlined,
+// their 32-value blocks and bias loads crowded the main epilogue loop's
+// registers in every kernel variant.
+__device__ __noinline__ float softmax_row_max(uint32_t t_row, int c0, int c1, int lim, float alpha,
+                                              const float* brow, int64_t bcs)
+{
+    float mx = -INFINITY;
+    for (int c = c0; c < c1 && c < lim; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int n = c + j;
+            if (n < lim) {
+                float x = alpha * __uint_as_float(r[j]);
+                if (brow) x += brow[(int64_t)n * bcs];
+                mx = fmaxf(mx, x);
+            }
+        }
+    }
+    return mx;
+}
+
+// exp(logit - mx) back into the row's columns [c0, min(c1, ncols)) (0 for
+// the -inf columns); returns their sum, accumulated in column order.
+__device__ __noinline__ float softmax_row_exp(uint32_t t_row, int c0, int c1, int ncols, int lim, float alpha,
+                                              const float* brow, int64_t bcs, float mx)
+{
+    float sum = 0.f;
+    for (int c = c0; c < c1 && c < ncols; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int n = c + j;
+            float e = 0.f;
+            if (n < lim) {
+                float x = alpha * __uint_as_float(r[j]);
+                if (brow) x += brow[(int64_t)n * bcs];
+                if (x != -INFINITY) e = expf(x - mx);
+            }
+            sum += e;
+            r[j] = __float_as_uint(e);
+        }
+        tmem_st32_async(t_row + c, r);
+    }
+    tmem_wait_st();   // the exps are in TMEM before the scaling pass reads them
+    return sum;
+}
+
 // tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
 // tmBlo map their lo planes (same layout), which the producer loads next to
 // the raw tiles instead of the split warps computing them.
@@ -996,43 +1049,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool causal = (p.epi & kEpiCausal) != 0;
                 float* xch = stage_w;                                                    // my posts
                 const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;   // partner's
-                auto logit = [&](uint32_t bits, int gn) {
-                    float x = p.alpha * __uint_as_float(bits);
-                    if (has_bias && rok) x += brow[(int64_t)gn * p.bias_cs];
-                    if (causal && gn > gm) x = -INFINITY;
-                    return x;
-                };
                 // every epilogue thread of the CTA has arrived on `bar` this tile
                 auto rows_meet = [&](uint64_t* bar) {
                     mbar_arrive(smem_u32(bar));
                     const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueRows);
                     return __all_sync(0xffffffffu, met);
                 };
-                float mx = -INFINITY;
-                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_row + c, r);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (c + j < p.N) mx = fmaxf(mx, logit(r[j], c + j));
-                }
+                // live columns: [0, N), and up to the diagonal when causal
+                const int lim = causal ? min(p.N, gm + 1) : p.N;
+                const float* bias_row = has_bias && rok ? brow : nullptr;
+                float mx = softmax_row_max(t_row, 32 * c_lo, 32 * c_hi, lim, p.alpha, bias_row, p.bias_cs);
                 xch[lane] = mx;
                 if (!rows_meet(&ss->row_max)) { ok = false; break; }
                 mx = fmaxf(mx, pxch[lane]);
-                float sum = 0.f;
-                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_row + c, r);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float x = c + j < p.N ? logit(r[j], c + j) : -INFINITY;
-                        const float e = x == -INFINITY ? 0.f : expf(x - mx);
-                        sum += e;
-                        r[j] = __float_as_uint(e);
-                    }
-                    tmem_st32_async(t_row + c, r);
-                }
-                tmem_wait_st();   // the exps are in TMEM before the scaling pass reads them
+                float sum = softmax_row_exp(t_row, 32 * c_lo, 32 * c_hi, p.N, lim, p.alpha, bias_row, p.bias_cs, mx);
                 xch[32 + lane] = sum;
                 if (!rows_meet(&ss->row_sum)) { ok = false; break; }
                 // the row's sum: first half's columns, then the second half's
