@@ -2,9 +2,11 @@
 
 Workload: C = A @ B, A and B [8192, 8192] fp32 ~ U(-1, 1). The rows of A (and
 so of C) are split across the N ranks (one process per GPU), B is replicated,
-and when N > 1 every GPU ends the step holding all of C: by default each rank's
-GEMM epilogue writes its rows into every GPU's C over NVLink (the all-gather
-fused into the kernel; --gather nccl uses an NCCL all-gather after the GEMM).
+and when N > 1 every GPU ends the step holding all of C: by default the GEMM
+kernel copies each finished tile into every GPU's C over NVLink (the
+all-gather fused into the kernel); --gather ce computes the rows in column
+bands and has the copy engines send each finished band beside the next one's
+GEMM; --gather nccl uses an NCCL all-gather after the GEMM.
 Work is fixed as N grows ("strong" scaling). Default mode 3xTF32
 (fp32-accurate); --mode tf32 times the fast mode.
 
@@ -56,10 +58,15 @@ def parse_args():
                         "batched / linear / attention: the one-GPU forward + backward GEMM workloads "
                         "(batched A[8,256,384] @ W[384,384]; linear layer X[16384,384] @ W[1536,384]^T + b; "
                         "causal attention Q, K, V [64,6,256,64] with the softmax fused)")
-    p.add_argument("--gather", choices=["fused", "nccl"], default="fused",
-                   help="N>1: C rows reach every GPU from the GEMM epilogue over NVLink (fused) "
-                        "or by an NCCL all-gather after it")
+    p.add_argument("--gather", choices=["fused", "ce", "nccl"], default="fused",
+                   help="N>1: C rows reach every GPU from the GEMM kernel over NVLink (fused), by the "
+                        "copy engines band by band beside the GEMM (ce), or by an NCCL all-gather after it")
     return p.parse_args()
+
+
+GATHER_NAMES = {"fused": " + all-gather fused into the GEMM kernel (NVLink peer stores)",
+                "ce": " + all-gather by the copy engines, column band by band beside the GEMM",
+                "nccl": " + NCCL all-gather"}
 
 
 def env_rank():
@@ -247,7 +254,10 @@ def main():
     C_local = torch.empty(rows, n, device=dev)
     C_full = torch.empty(n, n, device=dev) if world > 1 else C_local
     stream = torch.cuda.current_stream(dev)
-    fused = world > 1 and args.gather == "fused"
+    fused = world > 1 and args.gather in ("fused", "ce")
+    if fused:
+        # the library reads its export switch at every call
+        os.environ["MG_GEMM_EXPORT"] = "2" if args.gather == "ce" else os.environ.get("MG_GEMM_EXPORT", "1")
     peers = PeerRows(C_full) if fused else None
     fence = torch.zeros(1, device=dev)
 
@@ -411,8 +421,7 @@ def main():
         "data": "synthetic U(-1,1) (torch generator, seeded), resident in HBM",
         "config": {"workload": WORKLOAD, "size": n, "rows_per_gpu": rows,
                    "mode": args.mode,
-                   "parallelism": f"row-shard x{world}" + ((" + all-gather fused into the GEMM epilogue (NVLink peer stores)"
-                                                              if fused else " + NCCL all-gather") if world > 1 else ""),
+                   "parallelism": f"row-shard x{world}" + (GATHER_NAMES[args.gather] if world > 1 else ""),
                    "l2": "inputs larger than L2 (2 x 268 MB operands, 268 MB output)"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak, "traffic": traffic,

@@ -50,6 +50,11 @@ struct DeviceState {
     int max_clusters[4] = {0, 0, 0, 0};               // resident CTA pairs, per pair-kernel tile width
     int* status = nullptr;   // device address of g_device_status
     cudaMemPool_t pool = nullptr;   // the library's own stream-ordered pool (workspace)
+    // the copy-engine all-gather: a stream per destination, an event per band
+    bool copy_ready = false;
+    cudaStream_t copy_stream[mg::kMaxPeers] = {};
+    cudaEvent_t band_done[mg::kMaxBands] = {};
+    cudaEvent_t copies_done[mg::kMaxPeers] = {};
 };
 DeviceState g_dev[kMaxDevices];
 
@@ -159,6 +164,22 @@ mg_status device_state(DeviceState** out)
         }
     }
     *out = &d;
+    return MG_OK;
+}
+
+// Streams and events of the copy-engine all-gather, made on first use.
+mg_status copy_engine_state(DeviceState* d)
+{
+    if (d->copy_ready) return MG_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (d->copy_ready) return MG_OK;
+    for (int q = 0; q < mg::kMaxPeers; ++q) {
+        if (!d->copy_stream[q]) MG_CUDA_TRY(cudaStreamCreateWithFlags(&d->copy_stream[q], cudaStreamNonBlocking));
+        if (!d->copies_done[q]) MG_CUDA_TRY(cudaEventCreateWithFlags(&d->copies_done[q], cudaEventDisableTiming));
+    }
+    for (int b = 0; b < mg::kMaxBands; ++b)
+        if (!d->band_done[b]) MG_CUDA_TRY(cudaEventCreateWithFlags(&d->band_done[b], cudaEventDisableTiming));
+    d->copy_ready = true;
     return MG_OK;
 }
 
@@ -882,7 +903,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     // epilogue never waits on NVLink. Needs one destination in this process's
     // own memory (not mapped from another rank).
     int local = -1;
-    if (scatter && tuning_int("MG_GEMM_EXPORT", 1, 0, 1)) {
+    if (scatter && tuning_int("MG_GEMM_EXPORT", 1, 0, 2) != 0) {
         for (int q = 0; q < scatter->npeers && local < 0; ++q)
             if (!ipc_imported(scatter->peers[q])) local = q;
     }
@@ -1089,6 +1110,67 @@ mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const in
     return gemm_impl(&d, out, A, B, nullptr, stream, g_noalloc_ptr[dev], MG_NOALLOC_SCRATCH_BYTES);
 }
 
+// Copy-engine form of the row-sharded GEMM (MG_GEMM_EXPORT=2). The rank's
+// rows are computed band by band (mg::plan_bands: whole 256-wide tile
+// columns, one launch each) into this GPU's own full C; when a band is done,
+// every other rank's C receives it by cudaMemcpy2DAsync on a stream per
+// destination, so the copies run on the copy engines beside the next band's
+// GEMM and no SM issues a remote store. The caller's stream waits for the
+// copies before this returns, as it waits for the fused forms' kernel.
+static mg_status scatter_by_bands(const mg_gemm_desc* d, const float* A, const float* B, const float* bias,
+                                  const ScatterSpec& sc, int local, cudaStream_t st)
+{
+    DeviceState* dev = nullptr;
+    mg_status s = device_state(&dev);
+    if (s != MG_OK) return s;
+    s = copy_engine_state(dev);
+    if (s != MG_OK) return s;
+    const bool pair = use_pair(d->M);
+    const int tile_rows = pair ? 2 * mg::kBM : mg::kBM;
+    const int m_tiles = (int)((d->M + tile_rows - 1) / tile_rows);
+    const int n_tiles = (int)((d->N + 255) / 256);
+    mg::BandPlan bp;
+    mg::plan_bands(bp, m_tiles, n_tiles, pair ? dev->sm_count / 2 : dev->sm_count,
+                   tuning_int("MG_GEMM_BAND_COLS", 0, 1, 1 << 20));
+    const int64_t ld = d->ldc;
+    const size_t pitch = (size_t)ld * sizeof(float);
+    float* own = sc.peers[local] + sc.row0 * ld;
+    mg_status result = MG_OK;
+    for (int b = 0; b < bp.nbands; ++b) {
+        const int64_t c0 = (int64_t)bp.col0[b] * 256;
+        const int64_t c1 = std::min<int64_t>(d->N, (int64_t)bp.col0[b + 1] * 256);
+        mg_gemm_desc db = *d;
+        db.N = (int32_t)(c1 - c0);
+        const float* Bb = B + (d->trans_b ? c0 * d->ldb : c0);
+        const float* biasb = (d->epilogue & MG_EPI_BIAS) ? bias + c0 * d->bias_cs : bias;
+        result = gemm_impl(&db, own + c0, A, Bb, biasb, st, nullptr, 0);
+        if (result != MG_OK) break;
+        cudaError_t e = cudaEventRecord(dev->band_done[b], st);
+        for (int q = 0; q < sc.npeers && e == cudaSuccess; ++q) {
+            if (q == local) continue;
+            e = cudaStreamWaitEvent(dev->copy_stream[q], dev->band_done[b], 0);
+            if (e == cudaSuccess)
+                e = cudaMemcpy2DAsync(sc.peers[q] + sc.row0 * ld + c0, pitch, own + c0, pitch,
+                                      (size_t)(c1 - c0) * sizeof(float), (size_t)d->M, cudaMemcpyDeviceToDevice,
+                                      dev->copy_stream[q]);
+        }
+        if (e != cudaSuccess) {
+            result = fail(MG_ERR_CUDA, "copy of band %d to the other ranks failed: %s", b, cudaGetErrorString(e));
+            break;
+        }
+    }
+    // the caller's stream continues once every copy enqueued above has landed
+    // (also after a failure, so that nothing is left in flight behind it)
+    for (int q = 0; q < sc.npeers; ++q) {
+        if (q == local) continue;
+        cudaError_t e = cudaEventRecord(dev->copies_done[q], dev->copy_stream[q]);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(st, dev->copies_done[q], 0);
+        if (e != cudaSuccess && result == MG_OK)
+            result = fail(MG_ERR_CUDA, "joining the copy streams failed: %s", cudaGetErrorString(e));
+    }
+    return result;
+}
+
 mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const float* B, const float* bias,
                                float* const* peer_C, int32_t npeers, int64_t row0, int64_t rows_full,
                                void* stream)
@@ -1111,6 +1193,20 @@ mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const floa
         sc.peers[q] = peer_C[q];
     }
     if (d->K == 0) return fail(MG_ERR_UNSUPPORTED, "K = 0 is not supported by the scattering GEMM");
+    // copy engines instead of the kernel's export warps: a 2-D C without a
+    // row epilogue (bands cut the rows), one destination in this process
+    if (tuning_int("MG_GEMM_EXPORT", 1, 0, 2) == 2 && d->batch_rank == 0 &&
+        (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) == 0) {
+        int local = -1;
+        for (int q = 0; q < npeers && local < 0; ++q)
+            if (!ipc_imported(peer_C[q])) local = q;
+        if (local >= 0) {
+            mg_status s = validate(d, peer_C[local] + row0 * d->ldc, A, B, bias);
+            if (s != MG_OK) return s;
+            if (d->M == 0 || d->N == 0) return MG_OK;
+            return scatter_by_bands(d, A, B, bias, sc, local, (cudaStream_t)stream);
+        }
+    }
     return gemm_impl(d, peer_C[0], A, B, bias, stream, nullptr, 0, &sc);
 }
 

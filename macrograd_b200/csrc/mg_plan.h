@@ -1,4 +1,5 @@
-// mg_plan.h -- the GEMM kernel's work units and the K split of its last wave.
+// mg_plan.h -- the GEMM kernel's work units, the K split of its last wave, and
+// the column bands of the copy-engine all-gather.
 //
 // Plain C++ shared by the kernel (device), the launcher (host) and the CPU
 // tests (tests/plan_check.cpp), so the tests check the code the GPU runs.
@@ -120,6 +121,53 @@ inline int plan_k_split(UnitPlan& w, int total_tiles, int units, int num_kb, int
     }
     w.nlev = n;
     return slot0;
+}
+
+// Column bands of a row-sharded GEMM whose rows reach the other ranks through
+// the copy engines: the GEMM runs as one launch per band of whole n-tile
+// columns (m_tiles x columns tiles), and a finished band is copied to the
+// peers while the next band computes. A band holds w waves of `units` tiles:
+// the smallest w <= 4 whose whole columns fill at least 95 % of them, else
+// the fullest. The columns left over go last, in a smaller band (its launch
+// may split it along K), so the copy that cannot overlap is the shortest.
+// Returns the number of bands; 1 when a single band holds the whole GEMM.
+// force_cols > 0 sets the band width in columns instead (a tuning knob).
+constexpr int kMaxBands = 16;
+
+struct BandPlan {
+    int nbands;
+    int col0[kMaxBands + 1];   // band b: n-tile columns [col0[b], col0[b + 1])
+};
+
+inline int plan_bands(BandPlan& bp, int m_tiles, int n_tiles, int units, int force_cols = 0)
+{
+    bp.nbands = 1;
+    bp.col0[0] = 0;
+    bp.col0[1] = n_tiles;
+    if (m_tiles < 1 || n_tiles < 2 || units < 1) return 1;
+    int cols = 0;
+    double best = -1.0;
+    for (int w = 1; w <= 4; ++w) {
+        const int c = (int)((long long)w * units / m_tiles);
+        if (c < 1) continue;
+        const double fill = (double)c * m_tiles / ((double)w * units);
+        if (fill >= 0.95) {
+            cols = c;
+            break;
+        }
+        if (fill > best) {
+            best = fill;
+            cols = c;
+        }
+    }
+    if (cols < 1) cols = 1;   // a single column already holds more than 4 waves
+    if (force_cols > 0) cols = force_cols;
+    if (cols >= n_tiles) return 1;
+    int n = 0;
+    for (int c0 = 0; c0 < n_tiles && n < kMaxBands; c0 += cols) bp.col0[n++] = c0;
+    bp.col0[n] = n_tiles;   // past kMaxBands bands the last one takes the rest
+    bp.nbands = n;
+    return n;
 }
 
 }  // namespace mg

@@ -77,6 +77,40 @@ static int expect(int T, int U, int KB, int mk, int nlev, const int* split, cons
     return 0;
 }
 
+static int fail_bands(const char* what, int m, int n, int U)
+{
+    std::printf("FAIL %s (m-tiles %d, n-tiles %d, units %d)\n", what, m, n, U);
+    return 1;
+}
+
+// Column bands: contiguous, non-empty, cover every column once; all but the
+// last equally wide, the last no wider (unless the band cap merged the rest).
+static int check_bands(int m, int n, int U)
+{
+    mg::BandPlan bp;
+    const int nb = mg::plan_bands(bp, m, n, U);
+    if (nb != bp.nbands || nb < 1 || nb > mg::kMaxBands) return fail_bands("band count", m, n, U);
+    if (bp.col0[0] != 0 || bp.col0[nb] != n) return fail_bands("bands do not cover the columns", m, n, U);
+    for (int b = 0; b < nb; ++b)
+        if (bp.col0[b + 1] <= bp.col0[b]) return fail_bands("empty band", m, n, U);
+    const int w0 = bp.col0[1] - bp.col0[0];
+    for (int b = 0; b + 1 < nb; ++b)
+        if (bp.col0[b + 1] - bp.col0[b] != w0) return fail_bands("unequal bands", m, n, U);
+    if (nb > 1 && nb < mg::kMaxBands && bp.col0[nb] - bp.col0[nb - 1] > w0)
+        return fail_bands("last band wider than the others", m, n, U);
+    if (nb > 1 && (long long)w0 * m > 4ll * U && w0 > 1) return fail_bands("band above 4 waves", m, n, U);
+    return 0;
+}
+
+static int expect_bands(int m, int n, int U, int nb, const int* col0)
+{
+    mg::BandPlan bp;
+    if (mg::plan_bands(bp, m, n, U) != nb) return fail_bands("unexpected band count", m, n, U);
+    for (int b = 0; b <= nb; ++b)
+        if (bp.col0[b] != col0[b]) return fail_bands("unexpected band edge", m, n, U);
+    return 0;
+}
+
 int main()
 {
     int nsplit = 0;
@@ -98,6 +132,22 @@ int main()
     if (expect(256, 74, 256, 16, 1, s4, t4)) return 1;    // 4 GPUs: 3 waves + halves
     if (expect(1024, 74, 256, 16, 0, nullptr, nullptr)) return 1;   // 1 GPU: saves < 5 %
     if (nsplit == 0) return fail("no case split at all", 0, 0, 0, 0);
-    std::printf("ok %d split plans checked\n", nsplit);
+    int nbanded = 0;
+    for (int m = 1; m < 200; ++m)
+        for (int n = 1; n < 200; ++n)
+            for (int U : units) {
+                if (check_bands(m, n, U)) return 1;
+                mg::BandPlan bp;
+                nbanded += mg::plan_bands(bp, m, n, U) > 1;
+            }
+    // 8192^3 row-sharded over 8 / 4 / 2 GPUs: 256 x 256 pair tiles on 74 SM pairs
+    const int b8[] = {0, 18, 32}, b4[] = {0, 9, 18, 27, 32};
+    if (expect_bands(4, 32, 74, 2, b8)) return 1;     // 72 tiles (1 wave), then 56
+    if (expect_bands(8, 32, 74, 4, b4)) return 1;     // 3 x 72 tiles, then 40
+    if (expect_bands(16, 32, 74, 4, b4)) return 1;    // 3 x 144 tiles (2 waves each), then 80
+    const int one[] = {0, 16};
+    if (expect_bands(4, 16, 74, 1, one)) return 1;    // one wave: a single band
+    if (nbanded == 0) return fail_bands("no case banded at all", 0, 0, 0);
+    std::printf("ok %d split plans, %d band plans checked\n", nsplit, nbanded);
     return 0;
 }

@@ -5,8 +5,12 @@ runs in both of its forms: export warps copying finished tiles to the peer
 (default) and the epilogue storing to every rank itself (MG_GEMM_EXPORT=0);
 with the K split forced (MG_GEMM_SPLIT_MIN_KB=1) the last split level's rows
 go out through every CTA's export warps; a 1001-wide C takes the 4-byte copy
-paths. The NCCL gather of the same kernel's rows must be bit-identical. Skipped when fewer than 2 GPUs are
-visible."""
+paths. The NCCL gather of the same kernel's rows must be bit-identical. The
+copy-engine form (MG_GEMM_EXPORT=2: the GEMM in column bands, each band
+copied to the peer by cudaMemcpy2DAsync; forced to 256-column bands here, so
+that a 1024- or 1001-wide C makes four) may split bands along K where one
+launch does not, so its C is compared bit for bit with every rank's own rows
+broadcast over NCCL instead. Skipped when fewer than 2 GPUs are visible."""
 import os
 import socket
 
@@ -53,10 +57,12 @@ def _worker(rank, world, port, n, q):
         report = {}
         # (mode, export warps, K-split allowed down to this many K-blocks per range)
         for mode, export, min_kb in ((_lib.MG_MODE_TF32X3, "1", "16"), (_lib.MG_MODE_TF32, "1", "16"),
-                                     (_lib.MG_MODE_TF32X3, "0", "16"), (_lib.MG_MODE_TF32X3, "1", "1")):
+                                     (_lib.MG_MODE_TF32X3, "0", "16"), (_lib.MG_MODE_TF32X3, "1", "1"),
+                                     (_lib.MG_MODE_TF32X3, "2", "16"), (_lib.MG_MODE_TF32, "2", "1")):
             lib.mg_set_mode(mode)
             os.environ["MG_GEMM_EXPORT"] = export
             os.environ["MG_GEMM_SPLIT_MIN_KB"] = min_kb
+            os.environ["MG_GEMM_BAND_COLS"] = "1"    # bands of one 256-wide column: several copies
             full = torch.full((n, n), float("nan"), device=dev)
             peers = PeerRows(full)
             for _ in range(2):                       # two calls in a row into the same buffers
@@ -64,15 +70,24 @@ def _worker(rank, world, port, n, q):
                 fence = torch.zeros(1, device=dev)
                 dist.all_reduce(fence)                # every rank's kernel (and its remote rows) done
             torch.cuda.synchronize()
-            full_nccl = torch.empty((n, n), device=dev)
-            sharded_matmul(A_local, Bg, full_out=full_nccl)
-            torch.cuda.synchronize()
             got = full.cpu().numpy()
+            if export == "2":
+                same = True
+                for src in range(world):   # the rows each rank computed, as it holds them
+                    s0, s1 = row_block(n, world, src)
+                    own = full[s0:s1].clone()
+                    dist.broadcast(own, src)
+                    same = same and bool(torch.equal(own, full[s0:s1]))
+            else:
+                full_nccl = torch.empty((n, n), device=dev)
+                sharded_matmul(A_local, Bg, full_out=full_nccl)
+                torch.cuda.synchronize()
+                same = bool(np.array_equal(got, full_nccl.cpu().numpy()))
             rows = [0, 5, n // 2 - 1, n // 2, n // 2 + 7, n - 1]
             ref = ob.oracle_matmul(A[rows], B)
             tol = 1e-5 if mode == _lib.MG_MODE_TF32X3 else 2e-3
             report[(mode, export, min_kb)] = (bool(np.all(np.isfinite(got))), ob.frob_rel_err(got[rows], ref) <= tol,
-                            bool(np.array_equal(got, full_nccl.cpu().numpy())))
+                                              same)
             dist.barrier()
             peers.close()
         q.put((rank, report))
@@ -104,4 +119,4 @@ def test_fused_all_gather_on_two_gpus(n):
             what = f"rank {rank} mode {mode} export {export} split min_kb {min_kb}"
             assert finite, f"{what}: C has rows nobody wrote"
             assert close, f"{what}: rows differ from the oracle"
-            assert same, f"{what}: fused and NCCL all-gather differ"
+            assert same, f"{what}: gathered rows differ from the rows their rank computed"
