@@ -1130,7 +1130,11 @@ static mg_status scatter_by_bands(const mg_gemm_desc* d, const float* A, const f
     const int m_tiles = (int)((d->M + tile_rows - 1) / tile_rows);
     const int n_tiles = (int)((d->N + 255) / 256);
     mg::BandPlan bp;
-    mg::plan_bands(bp, m_tiles, n_tiles, pair ? dev->sm_count / 2 : dev->sm_count,
+    // the deepest K split a band's launch can make (as plan_split allows it)
+    const int num_kb = (int)((d->K + mg::kBK - 1) / mg::kBK);
+    const int min_kb = tuning_int("MG_GEMM_SPLIT", 1, 0, 1) ? tuning_int("MG_GEMM_SPLIT_MIN_KB", 16, 1, 1 << 20) : 0;
+    const int max_split = min_kb > 0 ? std::max(1, num_kb / min_kb) : 1;
+    mg::plan_bands(bp, m_tiles, n_tiles, pair ? dev->sm_count / 2 : dev->sm_count, max_split,
                    tuning_int("MG_GEMM_BAND_COLS", 0, 1, 1 << 20));
     const int64_t ld = d->ldc;
     const size_t pitch = (size_t)ld * sizeof(float);

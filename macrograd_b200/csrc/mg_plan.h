@@ -126,10 +126,16 @@ inline int plan_k_split(UnitPlan& w, int total_tiles, int units, int num_kb, int
 // Column bands of a row-sharded GEMM whose rows reach the other ranks through
 // the copy engines: the GEMM runs as one launch per band of whole n-tile
 // columns (m_tiles x columns tiles), and a finished band is copied to the
-// peers while the next band computes. A band holds w waves of `units` tiles:
-// the smallest w <= 4 whose whole columns fill at least 95 % of them, else
-// the fullest. The columns left over go last, in a smaller band (its launch
-// may split it along K), so the copy that cannot overlap is the shortest.
+// peers while the next band computes, so only the last band's copy is not
+// overlapped. Full bands hold w waves of `units` tiles: the smallest w <= 4
+// whose whole columns fill at least 95 % of them, else the fullest. When the
+// launches can split tiles along K (max_split >= 2: a tile's K-blocks make at
+// least two ranges of the shortest length), the columns after the full bands
+// -- or the last full band, when there are none left over -- are cut into
+// bands of about units / 2^k tiles, k = 1, 2, ... (2^k <= max_split), each
+// of which its launch can spread over every unit by a 2^k-way split; the
+// bands shrink towards the end and the last one is a single column at best.
+// Without the split the leftover columns form one last band.
 // Returns the number of bands; 1 when a single band holds the whole GEMM.
 // force_cols > 0 sets the band width in columns instead (a tuning knob).
 constexpr int kMaxBands = 16;
@@ -139,7 +145,7 @@ struct BandPlan {
     int col0[kMaxBands + 1];   // band b: n-tile columns [col0[b], col0[b + 1])
 };
 
-inline int plan_bands(BandPlan& bp, int m_tiles, int n_tiles, int units, int force_cols = 0)
+inline int plan_bands(BandPlan& bp, int m_tiles, int n_tiles, int units, int max_split = 1, int force_cols = 0)
 {
     bp.nbands = 1;
     bp.col0[0] = 0;
@@ -161,11 +167,34 @@ inline int plan_bands(BandPlan& bp, int m_tiles, int n_tiles, int units, int for
         }
     }
     if (cols < 1) cols = 1;   // a single column already holds more than 4 waves
+    const bool taper = force_cols <= 0 && max_split >= 2;
     if (force_cols > 0) cols = force_cols;
-    if (cols >= n_tiles) return 1;
-    int n = 0;
-    for (int c0 = 0; c0 < n_tiles && n < kMaxBands; c0 += cols) bp.col0[n++] = c0;
-    bp.col0[n] = n_tiles;   // past kMaxBands bands the last one takes the rest
+    if (cols >= n_tiles && !taper) return 1;
+    int full = n_tiles / cols, rem = n_tiles - full * cols;
+    if (taper && rem == 0) {   // the last full band tapers instead
+        --full;
+        rem = cols;
+    }
+    if (full > kMaxBands - 1) full = kMaxBands - 1;
+    rem = n_tiles - full * cols;
+    int n = 0, c = 0;
+    for (; n < full; ++n, c += cols) bp.col0[n] = c;
+    for (int k = taper ? 1 : 0; rem > 0;) {
+        long long t = rem;
+        if (taper && k < 30 && (1 << k) <= max_split) {
+            t = units / ((long long)m_tiles << k);
+            if (t >= rem) {   // a smaller band first
+                ++k;
+                continue;
+            }
+            if (t < 1) t = rem;
+        }
+        if (n == kMaxBands - 1) t = rem;   // past the band limit the last one takes the rest
+        bp.col0[n++] = c;
+        c += (int)t;
+        rem -= (int)t;
+    }
+    bp.col0[n] = n_tiles;
     bp.nbands = n;
     return n;
 }

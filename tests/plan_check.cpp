@@ -83,29 +83,33 @@ static int fail_bands(const char* what, int m, int n, int U)
     return 1;
 }
 
-// Column bands: contiguous, non-empty, cover every column once; all but the
-// last equally wide, the last no wider (unless the band cap merged the rest).
-static int check_bands(int m, int n, int U)
+// Column bands: contiguous, non-empty, cover every column once; widths never
+// grow towards the end (unless the band cap merged the rest into the last);
+// the first band holds at most 4 waves (or one column).
+static int check_bands(int m, int n, int U, int ms)
 {
     mg::BandPlan bp;
-    const int nb = mg::plan_bands(bp, m, n, U);
+    const int nb = mg::plan_bands(bp, m, n, U, ms);
     if (nb != bp.nbands || nb < 1 || nb > mg::kMaxBands) return fail_bands("band count", m, n, U);
     if (bp.col0[0] != 0 || bp.col0[nb] != n) return fail_bands("bands do not cover the columns", m, n, U);
     for (int b = 0; b < nb; ++b)
         if (bp.col0[b + 1] <= bp.col0[b]) return fail_bands("empty band", m, n, U);
+    const int last = nb < mg::kMaxBands ? nb : nb - 1;   // bands that must not grow
+    for (int b = 1; b < last; ++b)
+        if (bp.col0[b + 1] - bp.col0[b] > bp.col0[b] - bp.col0[b - 1]) return fail_bands("band wider than the one before", m, n, U);
     const int w0 = bp.col0[1] - bp.col0[0];
-    for (int b = 0; b + 1 < nb; ++b)
-        if (bp.col0[b + 1] - bp.col0[b] != w0) return fail_bands("unequal bands", m, n, U);
-    if (nb > 1 && nb < mg::kMaxBands && bp.col0[nb] - bp.col0[nb - 1] > w0)
-        return fail_bands("last band wider than the others", m, n, U);
     if (nb > 1 && (long long)w0 * m > 4ll * U && w0 > 1) return fail_bands("band above 4 waves", m, n, U);
+    if (ms < 2 && nb > 1) {   // no split: equal bands, then the leftover
+        for (int b = 0; b + 1 < nb; ++b)
+            if (bp.col0[b + 1] - bp.col0[b] != w0) return fail_bands("unequal full bands", m, n, U);
+    }
     return 0;
 }
 
-static int expect_bands(int m, int n, int U, int nb, const int* col0)
+static int expect_bands(int m, int n, int U, int ms, int nb, const int* col0)
 {
     mg::BandPlan bp;
-    if (mg::plan_bands(bp, m, n, U) != nb) return fail_bands("unexpected band count", m, n, U);
+    if (mg::plan_bands(bp, m, n, U, ms) != nb) return fail_bands("unexpected band count", m, n, U);
     for (int b = 0; b <= nb; ++b)
         if (bp.col0[b] != col0[b]) return fail_bands("unexpected band edge", m, n, U);
     return 0;
@@ -133,20 +137,25 @@ int main()
     if (expect(1024, 74, 256, 16, 0, nullptr, nullptr)) return 1;   // 1 GPU: saves < 5 %
     if (nsplit == 0) return fail("no case split at all", 0, 0, 0, 0);
     int nbanded = 0;
-    for (int m = 1; m < 200; ++m)
-        for (int n = 1; n < 200; ++n)
-            for (int U : units) {
-                if (check_bands(m, n, U)) return 1;
-                mg::BandPlan bp;
-                nbanded += mg::plan_bands(bp, m, n, U) > 1;
-            }
-    // 8192^3 row-sharded over 8 / 4 / 2 GPUs: 256 x 256 pair tiles on 74 SM pairs
-    const int b8[] = {0, 18, 32}, b4[] = {0, 9, 18, 27, 32};
-    if (expect_bands(4, 32, 74, 2, b8)) return 1;     // 72 tiles (1 wave), then 56
-    if (expect_bands(8, 32, 74, 4, b4)) return 1;     // 3 x 72 tiles, then 40
-    if (expect_bands(16, 32, 74, 4, b4)) return 1;    // 3 x 144 tiles (2 waves each), then 80
-    const int one[] = {0, 16};
-    if (expect_bands(4, 16, 74, 1, one)) return 1;    // one wave: a single band
+    for (int m = 1; m < 160; ++m)
+        for (int n = 1; n < 160; ++n)
+            for (int U : units)
+                for (int ms : {1, 2, 8, 16}) {
+                    if (check_bands(m, n, U, ms)) return 1;
+                    mg::BandPlan bp;
+                    nbanded += mg::plan_bands(bp, m, n, U, ms) > 1;
+                }
+    // 8192^3 row-sharded over 8 / 4 / 2 GPUs: 256 x 256 pair tiles on 74 SM pairs,
+    // 256 K-blocks (up to a 16-way split at the default 16-block minimum)
+    const int b8[] = {0, 18, 27, 31, 32}, b8s[] = {0, 18, 32};
+    const int b4[] = {0, 9, 18, 27, 31, 32}, b2[] = {0, 9, 18, 27, 29, 31, 32};
+    if (expect_bands(4, 32, 74, 16, 4, b8)) return 1;     // 72 tiles (1 wave), 36, 16, 4
+    if (expect_bands(4, 32, 74, 1, 2, b8s)) return 1;     // no K split: 72, then the 56 left
+    if (expect_bands(8, 32, 74, 16, 5, b4)) return 1;     // 3 x 72 tiles, 32, 8
+    if (expect_bands(16, 32, 74, 16, 6, b2)) return 1;    // 3 x 144 tiles (2 waves), 32, 32, 16
+    const int one[] = {0, 16}, taper1[] = {0, 9, 13, 15, 16};
+    if (expect_bands(4, 16, 74, 1, 1, one)) return 1;     // one wave, no split: a single band
+    if (expect_bands(4, 16, 74, 16, 4, taper1)) return 1; // one wave, split: 36, 16, 8, 4 tiles
     if (nbanded == 0) return fail_bands("no case banded at all", 0, 0, 0);
     std::printf("ok %d split plans, %d band plans checked\n", nsplit, nbanded);
     return 0;
