@@ -4,7 +4,8 @@ kernel and the launcher compile is built into tests/plan_check.cpp with g++
 and run over thousands of (tiles, units, K-blocks) cases -- every (tile,
 K-block) covered once, partial slots written once and read by their tile's
 final range, the split never slower than whole-tile waves -- plus the plans
-of the row-sharded 8192^3 shapes."""
+of the row-sharded 8192^3 shapes, and the column bands of the copy-engine
+all-gather (contiguous, covering, never growing towards the end)."""
 import os
 import shutil
 import subprocess
