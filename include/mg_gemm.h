@@ -141,17 +141,22 @@ mg_status mg_matmul_softmax_backward(float* dS, const float* A, const float* B, 
 /* ---- multi-GPU: row-sharded GEMM with the all-gather fused into it ------
  * No counterpart in the reference (single-GPU only, README.md:538). A job of
  * R ranks (one process per GPU) splits the rows of A (and of C) into R blocks;
- * B is replicated. Each rank runs mg_gemm_scatter_rows on its rows, and its
- * epilogue writes every finished row chunk straight into the full C of every
- * rank (peer_C[0..npeers), this rank's own included) at row row0 + m, over
- * NVLink peer mappings -- so the all-gather travels while the tensor cores
- * work, instead of after. No collective runs inside the kernel; the caller
- * orders steps across ranks (e.g. a small NCCL all-reduce after the GEMM)
- * before reading a C that other ranks write into, or overwriting it again.
- * `d` describes this rank's GEMM (M = its rows); d->ldc is the row stride of
- * the full C buffers, which have rows_full rows; beta must be 0. For a 2-D C
- * the remote rows leave as TMA bulk tensor stores, so the copies run on the
- * TMA engine while the warps go on. */
+ * B is replicated. Each rank runs mg_gemm_scatter_rows on its rows, and every
+ * finished tile of them reaches the full C of every rank (peer_C[0..npeers),
+ * this rank's own included) at row row0 + m, over NVLink peer mappings -- so
+ * the all-gather travels while the tensor cores work, instead of after. By
+ * default the epilogue writes the tile into this rank's own C and the
+ * kernel's export warps copy it on to the other ranks (MG_GEMM_EXPORT=0: the
+ * epilogue stores every rank's copy itself; MG_GEMM_EXPORT=2: the rows are
+ * computed in column bands, one launch each, and the copy engines send each
+ * finished band while the next one computes; the call returns with `stream`
+ * ordered after those copies). The export-warp and copy-engine forms need
+ * one of peer_C in this process's own memory. No collective runs inside the
+ * kernel; the caller orders steps across ranks (e.g. a small NCCL all-reduce
+ * after the GEMM) before reading a C that other ranks write into, or
+ * overwriting it again. `d` describes this rank's GEMM (M = its rows);
+ * d->ldc is the row stride of the full C buffers, which have rows_full rows;
+ * beta must be 0. */
 #define MG_MAX_PEERS 8
 mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const float* B,
                                const float* bias, float* const* peer_C, int32_t npeers,
