@@ -39,11 +39,11 @@ __device__ int g_device_status[2];
 // GPU that loads this library, held until the process exits. In host code this
 // name is only a handle for cudaGetSymbolAddress, never a device address.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[MG_NOALLOC_SCRATCH_BYTES];
-uint8_t* g_noalloc_ptr[64] = {nullptr};   // its device address, per device ordinal
+std::atomic<uint8_t*> g_noalloc_ptr[64];   // its device address, per device ordinal (null: not yet)
 
 constexpr int kMaxDevices = 64;
 struct DeviceState {
-    bool ready = false;
+    std::atomic<bool> ready{false};   // set last, under g_mu (read without it)
     int sm_count = 0;
     int max_smem = 0;
     size_t attr_smem[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // dynamic smem opted in, per kernel variant
@@ -51,7 +51,7 @@ struct DeviceState {
     int* status = nullptr;   // device address of g_device_status
     cudaMemPool_t pool = nullptr;   // the library's own stream-ordered pool (workspace)
     // the copy-engine all-gather: a stream per destination, an event per band
-    bool copy_ready = false;
+    std::atomic<bool> copy_ready{false};
     cudaStream_t copy_stream[mg::kMaxPeers] = {};
     cudaEvent_t band_done[mg::kMaxBands] = {};
     cudaEvent_t copies_done[mg::kMaxPeers] = {};
@@ -127,9 +127,9 @@ mg_status device_state(DeviceState** out)
     MG_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return fail(MG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
     DeviceState& d = g_dev[dev];
-    if (!d.ready) {
+    if (!d.ready.load(std::memory_order_acquire)) {
         std::lock_guard<std::mutex> lk(g_mu);
-        if (!d.ready) {
+        if (!d.ready.load(std::memory_order_relaxed)) {
             cudaDeviceProp prop;
             MG_CUDA_TRY(cudaGetDeviceProperties(&prop, dev));
             if (prop.major != 10)
@@ -160,7 +160,7 @@ mg_status device_state(DeviceState** out)
             MG_CUDA_TRY(cudaMemPoolCreate(&d.pool, &pp));
             uint64_t keep = ~0ull;
             MG_CUDA_TRY(cudaMemPoolSetAttribute(d.pool, cudaMemPoolAttrReleaseThreshold, &keep));
-            d.ready = true;
+            d.ready.store(true, std::memory_order_release);
         }
     }
     *out = &d;
@@ -170,16 +170,16 @@ mg_status device_state(DeviceState** out)
 // Streams and events of the copy-engine all-gather, made on first use.
 mg_status copy_engine_state(DeviceState* d)
 {
-    if (d->copy_ready) return MG_OK;
+    if (d->copy_ready.load(std::memory_order_acquire)) return MG_OK;
     std::lock_guard<std::mutex> lk(g_mu);
-    if (d->copy_ready) return MG_OK;
+    if (d->copy_ready.load(std::memory_order_relaxed)) return MG_OK;
     for (int q = 0; q < mg::kMaxPeers; ++q) {
         if (!d->copy_stream[q]) MG_CUDA_TRY(cudaStreamCreateWithFlags(&d->copy_stream[q], cudaStreamNonBlocking));
         if (!d->copies_done[q]) MG_CUDA_TRY(cudaEventCreateWithFlags(&d->copies_done[q], cudaEventDisableTiming));
     }
     for (int b = 0; b < mg::kMaxBands; ++b)
         if (!d->band_done[b]) MG_CUDA_TRY(cudaEventCreateWithFlags(&d->band_done[b], cudaEventDisableTiming));
-    d->copy_ready = true;
+    d->copy_ready.store(true, std::memory_order_release);
     return MG_OK;
 }
 
@@ -1099,15 +1099,18 @@ mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const in
     int dev = 0;
     MG_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return fail(MG_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    uint8_t* scratch = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (scratch == nullptr) {
         std::lock_guard<std::mutex> lk(g_mu);
-        if (g_noalloc_ptr[dev] == nullptr) {
+        scratch = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+        if (scratch == nullptr) {
             void* p = nullptr;
             MG_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-            g_noalloc_ptr[dev] = static_cast<uint8_t*>(p);
+            scratch = static_cast<uint8_t*>(p);
+            g_noalloc_ptr[dev].store(scratch, std::memory_order_release);
         }
     }
-    return gemm_impl(&d, out, A, B, nullptr, stream, g_noalloc_ptr[dev], MG_NOALLOC_SCRATCH_BYTES);
+    return gemm_impl(&d, out, A, B, nullptr, stream, scratch, MG_NOALLOC_SCRATCH_BYTES);
 }
 
 // Copy-engine form of the row-sharded GEMM (MG_GEMM_EXPORT=2). The rank's
@@ -1219,14 +1222,16 @@ static_assert(sizeof(cudaIpcMemHandle_t) <= sizeof(mg_ipc_handle), "IPC handle d
 // The allocation containing a device pointer (driver cuMemGetAddressRange).
 static mg_status address_range(const void* p, CUdeviceptr* base, size_t* size)
 {
-    static PFN_cuMemGetAddressRange_v3020 get_range = nullptr;
-    if (!get_range) {
+    // looked up once (thread-safe static initialisation); null if unavailable
+    static const PFN_cuMemGetAddressRange_v3020 get_range = []() -> PFN_cuMemGetAddressRange_v3020 {
         void* fn = nullptr;
         cudaDriverEntryPointQueryResult q;
-        MG_CUDA_TRY(cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q));
-        if (q != cudaDriverEntryPointSuccess || !fn) return fail(MG_ERR_CUDA, "cuMemGetAddressRange unavailable");
-        get_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
-    }
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+    }();
+    if (!get_range) return fail(MG_ERR_CUDA, "cuMemGetAddressRange unavailable");
     if (get_range(base, size, (CUdeviceptr)p) != CUDA_SUCCESS)
         return fail(MG_ERR_INVALID, "pointer is not device memory");
     return MG_OK;
