@@ -263,7 +263,7 @@ def main():
 
     def gemm():
         if fused:
-            scatter_matmul(A, B, peers, r0)               # rows into every GPU's C, from the epilogue
+            scatter_matmul(A, B, peers, r0)               # rows into every GPU's C while the GEMM runs
         else:
             sharded_matmul(A, B, local_out=C_local)       # this rank's rows (one GEMM launch)
 

@@ -4,10 +4,12 @@ C = A @ B where the rows of A (and so of C) are split over the ranks and B is
 replicated. Rows of C depend only on the same rows of A, so each rank's GEMM is
 independent -- no collective inside the GEMM. When the caller needs the whole C
 on every device, the row blocks are all-gathered (NCCL over NVLink on GPUs,
-gloo on CPU in the tests), or -- the B200 path -- written by each rank's GEMM
-epilogue directly into every rank's C over NVLink peer mappings (PeerRows +
-scatter_matmul), so the exchange overlaps the math. The reference has no
-multi-device path; this is the row-sharded layer its matmul path gains here.
+gloo on CPU in the tests), or -- the B200 path -- sent by each rank's GEMM into
+every rank's C over NVLink peer mappings while it computes (PeerRows +
+scatter_matmul: the kernel's export warps copy each finished tile, or with
+MG_GEMM_EXPORT=2 the copy engines send each finished column band), so the
+exchange overlaps the math. The reference has no multi-device path; this is
+the row-sharded layer its matmul path gains here.
 """
 from __future__ import annotations
 
@@ -93,21 +95,34 @@ class PeerRows:
 
 def scatter_matmul(A_local: torch.Tensor, B: torch.Tensor, peers: PeerRows, row0: int,
                    stream: Optional[torch.cuda.Stream] = None) -> None:
-    """This rank's rows of C = A @ B, written by the GEMM epilogue straight into
-    every rank's full C (all-gather fused into the kernel, mg_gemm_scatter_rows).
-    The caller orders it across ranks before C is read."""
+    """This rank's rows of C = A @ B, sent into every rank's full C (at rows
+    row0 ...) while the GEMM runs (mg_gemm_scatter_rows). A_local [M, K] and
+    B [K, N] are contiguous fp32 on this rank's GPU; peers.full is the [rows,
+    N] full C. The caller orders it across ranks before C is read."""
     from . import _lib
 
-    lib = _lib.load()
+    full = peers.full
+    for name, t in (("A_local", A_local), ("B", B), ("the full C", full)):
+        if t.dim() != 2 or t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+            raise ValueError(f"scatter_matmul: {name} must be a contiguous 2-D float32 CUDA tensor "
+                             f"(got {tuple(t.shape)}, {t.dtype}, {t.device}, contiguous={t.is_contiguous()})")
+    if A_local.device != B.device or A_local.device != full.device:
+        raise ValueError("scatter_matmul: A_local, B and the full C must be on one device")
     M, K = A_local.shape
     N = B.shape[1]
+    if B.shape[0] != K or full.shape[1] != N:
+        raise ValueError(f"scatter_matmul: shapes do not chain: A_local {tuple(A_local.shape)}, "
+                         f"B {tuple(B.shape)}, full C {tuple(full.shape)}")
+    if row0 < 0 or row0 + M > full.shape[0]:
+        raise ValueError(f"scatter_matmul: rows [{row0}, {row0 + M}) are outside the {full.shape[0]} rows of C")
+    lib = _lib.load()
     d = _lib.GemmDesc()
     lib.mg_gemm_desc_init(ctypes.byref(d), M, N, K, 0, 0)
-    d.ldc = peers.full.stride(0)
+    d.ldc = full.stride(0)
     s = stream if stream is not None else torch.cuda.current_stream(A_local.device)
     _lib.check(lib.mg_gemm_scatter_rows(ctypes.byref(d), ctypes.c_void_p(A_local.data_ptr()),
                                         ctypes.c_void_p(B.data_ptr()), None, peers.array, len(peers.ptrs),
-                                        int(row0), int(peers.full.shape[0]), ctypes.c_void_p(s.cuda_stream)))
+                                        int(row0), int(full.shape[0]), ctypes.c_void_p(s.cuda_stream)))
 
 
 def sharded_matmul(A_local: torch.Tensor, B: torch.Tensor, full_out: Optional[torch.Tensor] = None,

@@ -57,3 +57,22 @@ def test_view_layout_reads_strides_of_head_split_views():
     bad = torch.zeros(4, 6, 8)[:, ::2, ::2]
     with pytest.raises(F.MacrogradError):
         F.view_layout(bad.shape, bad.stride())
+
+
+def test_scatter_matmul_rejects_operands_it_cannot_describe():
+    """The row-sharded GEMM passes raw pointers with a contiguous row-major
+    descriptor, so anything else is refused before the library is called."""
+    import types
+
+    import torch
+
+    from macrograd_b200.sharded import scatter_matmul
+
+    peers = types.SimpleNamespace(full=torch.zeros(8, 6), array=None, ptrs=[])
+    A, B = torch.zeros(4, 5), torch.zeros(5, 6)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        scatter_matmul(A, B, peers, 0)                       # host tensors
+    with pytest.raises(ValueError, match="contiguous"):
+        scatter_matmul(torch.zeros(5, 4).t(), B, peers, 0)   # a transposed view
+    with pytest.raises(ValueError, match="float32"):
+        scatter_matmul(A.double(), B, peers, 0)
