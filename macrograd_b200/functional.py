@@ -96,6 +96,19 @@ def _stream_handle(t: torch.Tensor, stream: Optional[torch.cuda.Stream]):
     return ctypes.c_void_p(s.cuda_stream)
 
 
+def _one_device(*tensors, stream: Optional[torch.cuda.Stream] = None) -> torch.device:
+    """The one CUDA device all given tensors (None skipped) and the stream are
+    on: the library runs each call on the current device, so a call is made
+    under this one."""
+    devs = {t.device for t in tensors if t is not None}
+    if stream is not None:
+        devs.add(torch.device(stream.device))
+    if len(devs) != 1:
+        raise MacrogradError(_lib.MG_ERR_INVALID,
+                             "operands (and stream) are on different devices: " + ", ".join(sorted(map(str, devs))))
+    return next(iter(devs))
+
+
 def _check_operand(t: torch.Tensor, name: str):
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise MacrogradError(_lib.MG_ERR_INVALID, f"{name} must be a CUDA tensor")
@@ -115,21 +128,25 @@ def matmul(mat0: torch.Tensor, mat1: torch.Tensor, bias: Optional[torch.Tensor] 
     _check_operand(mat1, "mat1")
     if bias is not None:
         _check_operand(bias, "bias")
+    if out is not None:
+        _check_operand(out, "out")
+    dev = _one_device(mat0, mat1, bias, out, stream=stream)
     a, b, oshape, a1d, b1d = equalize(mat0.shape, mat1.shape, transA, transB)
     if out is None:
-        out = torch.empty(oshape, device=mat0.device, dtype=torch.float32)
-    elif list(out.shape) != oshape or not out.is_contiguous():
+        out = torch.empty(oshape, device=dev, dtype=torch.float32)
+    elif list(out.shape) != oshape:
         raise MacrogradError(_lib.MG_ERR_INVALID, f"out must be a contiguous tensor of shape {oshape}")
     rank = len(oshape)
     st = _stream_handle(mat0, stream)
-    if bias is None:
-        check(lib.mg_matmul(_ptr(out), _ptr(mat0), _ptr(mat1), i32_array(oshape), i32_array(a),
-                            i32_array(b), rank, int(transA), int(transB), st))
-    else:
-        bs = equalize_bias(bias.shape, oshape)
-        check(lib.mg_matmul_bias(_ptr(out), _ptr(mat0), _ptr(mat1), _ptr(bias), i32_array(oshape),
-                                 i32_array(a), i32_array(b), i32_array(bs), rank, int(transA),
-                                 int(transB), st))
+    with torch.cuda.device(dev):
+        if bias is None:
+            check(lib.mg_matmul(_ptr(out), _ptr(mat0), _ptr(mat1), i32_array(oshape), i32_array(a),
+                                i32_array(b), rank, int(transA), int(transB), st))
+        else:
+            bs = equalize_bias(bias.shape, oshape)
+            check(lib.mg_matmul_bias(_ptr(out), _ptr(mat0), _ptr(mat1), _ptr(bias), i32_array(oshape),
+                                     i32_array(a), i32_array(b), i32_array(bs), rank, int(transA),
+                                     int(transB), st))
     if a1d:
         out = out.squeeze(-2)
     if b1d:
@@ -148,13 +165,17 @@ def attention_scores(q: torch.Tensor, k: torch.Tensor, scale: float, causal: boo
     lib = _lib.load()
     _check_operand(q, "q")
     _check_operand(k, "k")
+    if mask is not None:
+        _check_operand(mask, "mask")
+    dev = _one_device(q, k, mask, stream=stream)
     a, b, oshape, _, _ = equalize(q.shape, k.shape, False, True)
-    out = torch.empty(oshape, device=q.device, dtype=torch.float32)
+    out = torch.empty(oshape, device=dev, dtype=torch.float32)
     bs = equalize_bias(mask.shape, oshape) if mask is not None else None
-    check(lib.mg_matmul_softmax(_ptr(out), _ptr(q), _ptr(k), _ptr(mask), i32_array(oshape),
-                                i32_array(a), i32_array(b), i32_array(bs) if bs else None,
-                                len(oshape), 0, 1, ctypes.c_float(scale), int(causal),
-                                _stream_handle(q, stream)))
+    with torch.cuda.device(dev):
+        check(lib.mg_matmul_softmax(_ptr(out), _ptr(q), _ptr(k), _ptr(mask), i32_array(oshape),
+                                    i32_array(a), i32_array(b), i32_array(bs) if bs else None,
+                                    len(oshape), 0, 1, ctypes.c_float(scale), int(causal),
+                                    _stream_handle(q, stream)))
     return out
 
 
@@ -169,13 +190,15 @@ def attention_softmax_backward(dO: torch.Tensor, v: torch.Tensor, p: torch.Tenso
     _check_operand(dO, "dO")
     _check_operand(v, "v")
     _check_operand(p, "p")
+    dev = _one_device(dO, v, p, stream=stream)
     a, b, oshape, _, _ = equalize(dO.shape, v.shape, False, True)
     if list(p.shape) != oshape:
         raise MacrogradError(_lib.MG_ERR_INVALID, f"p must have the product's shape {oshape}")
-    out = torch.empty(oshape, device=dO.device, dtype=torch.float32)
-    check(lib.mg_matmul_softmax_backward(_ptr(out), _ptr(dO), _ptr(v), _ptr(p), i32_array(oshape), i32_array(a),
-                                         i32_array(b), len(oshape), 0, 1, ctypes.c_float(alpha),
-                                         _stream_handle(dO, stream)))
+    out = torch.empty(oshape, device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        check(lib.mg_matmul_softmax_backward(_ptr(out), _ptr(dO), _ptr(v), _ptr(p), i32_array(oshape),
+                                             i32_array(a), i32_array(b), len(oshape), 0, 1, ctypes.c_float(alpha),
+                                             _stream_handle(dO, stream)))
     return out
 
 
@@ -241,8 +264,13 @@ def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = 
     if nb > _lib.MG_MAX_BATCH_DIMS:
         raise MacrogradError(_lib.MG_ERR_UNSUPPORTED, f"more than {_lib.MG_MAX_BATCH_DIMS} leading dims")
     oshape = batch + [M, N]
+    if out is not None and (not out.is_cuda or out.dtype != torch.float32):
+        raise MacrogradError(_lib.MG_ERR_INVALID, "out must be a float32 CUDA tensor")
+    if bias is not None:
+        _check_operand(bias, "bias")
+    dev = _one_device(a, b, out, bias, stream=stream)
     if out is None:
-        out = torch.empty(oshape, device=a.device, dtype=torch.float32)
+        out = torch.empty(oshape, device=dev, dtype=torch.float32)
     if list(out.shape) != oshape or out.stride(-1) != 1:
         raise MacrogradError(_lib.MG_ERR_INVALID, f"out must have shape {oshape} and unit column stride")
     d = _lib.GemmDesc()
@@ -256,7 +284,6 @@ def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = 
         d.c_batch_stride[i] = out.stride(i)
     d.alpha = alpha
     if bias is not None:
-        _check_operand(bias, "bias")
         bs = equalize_bias(bias.shape, oshape)
         d.epilogue = _lib.MG_EPI_BIAS
         # contiguous bias broadcast to out: element strides, 0 where broadcast
@@ -268,7 +295,8 @@ def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = 
         d.bias_rs, d.bias_cs = strides[-2], strides[-1]
         for i in range(nb):
             d.bias_batch_stride[i] = strides[i]
-    check(lib.mg_gemm(ctypes.byref(d), _ptr(out), _ptr(a), _ptr(b), _ptr(bias), _stream_handle(a, stream)))
+    with torch.cuda.device(dev):
+        check(lib.mg_gemm(ctypes.byref(d), _ptr(out), _ptr(a), _ptr(b), _ptr(bias), _stream_handle(a, stream)))
     return out
 
 
@@ -299,15 +327,20 @@ def _grad_gemm(X: torch.Tensor, Y: torch.Tensor, tX: bool, tY: bool, target_shap
     tensor_ops.cpp:3345-3451), optionally accumulated into `accumulate`."""
     folded = _fold_batch(list(X.shape), list(Y.shape), list(target_shape), tX, tY)
     lib = _lib.load()
-    st = _stream_handle(X, stream)
     if folded is not None:
+        _check_operand(X, "gradient operand")
+        _check_operand(Y, "gradient operand")
+        if accumulate is not None:
+            _check_operand(accumulate, "gradient accumulator")
+        dev = _one_device(X, Y, accumulate, stream=stream)
         xs, ys = folded
         oshape = [xs[-1], ys[-1]]
-        dst = accumulate if accumulate is not None else torch.empty(target_shape, device=X.device)
+        dst = accumulate if accumulate is not None else torch.empty(target_shape, device=dev, dtype=torch.float32)
         d = _lib.GemmDesc()
         lib.mg_gemm_desc_init(ctypes.byref(d), oshape[0], oshape[1], xs[0], 1, 0)
         d.beta = 1.0 if accumulate is not None else 0.0
-        check(lib.mg_gemm(ctypes.byref(d), _ptr(dst), _ptr(X), _ptr(Y), None, st))
+        with torch.cuda.device(dev):
+            check(lib.mg_gemm(ctypes.byref(d), _ptr(dst), _ptr(X), _ptr(Y), None, _stream_handle(X, stream)))
         return dst
     res = matmul(X, Y, None, tX, tY, stream=stream)
     if list(res.shape) != list(target_shape):
@@ -336,6 +369,9 @@ def matmul_backward(A: torch.Tensor, B: torch.Tensor, dC: torch.Tensor, transA: 
     broadcast over the batch (a weight) is one GEMM with the batch folded into
     K instead of a batched temporary plus a reduction. grad_a / grad_b, when
     given, are accumulated into (beta = 1) instead of freshly allocated."""
+    for name, g in (("grad_a", grad_a), ("grad_b", grad_b)):
+        if g is not None:
+            _check_operand(g, name)   # reshaped below as a view: the accumulation lands in it
     a, b, oshape, _, _ = equalize(A.shape, B.shape, transA, transB)
     Av = A.reshape(a)
     Bv = B.reshape(b)

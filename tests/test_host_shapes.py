@@ -76,3 +76,18 @@ def test_scatter_matmul_rejects_operands_it_cannot_describe():
         scatter_matmul(torch.zeros(5, 4).t(), B, peers, 0)   # a transposed view
     with pytest.raises(ValueError, match="float32"):
         scatter_matmul(A.double(), B, peers, 0)
+
+
+def test_calls_take_one_device():
+    """Every entry point runs on the one device all its tensors (and the
+    stream) are on; mixed devices are refused."""
+    import types
+
+    import torch
+
+    a = torch.zeros(2)
+    assert F._one_device(a, None, a) == torch.device("cpu")
+    with pytest.raises(MacrogradError, match="different devices"):
+        F._one_device(a, torch.zeros(2, device="meta"))
+    with pytest.raises(MacrogradError, match="different devices"):
+        F._one_device(a, stream=types.SimpleNamespace(device=torch.device("cuda", 0)))
