@@ -34,7 +34,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 SIZE = 8192
 METRIC = "fp32-accurate matmul TFLOP/s & % TF32 roofline at 1/2/4/8 B200 vs host CPU"
 UNIT = "TFLOP/s"
-WORKLOAD = "square fp32 GEMM 8192x8192x8192, rows of A sharded over the GPUs, C rows all-gathered"
+def workload(n):
+    return f"square fp32 GEMM {n}x{n}x{n}, rows of A sharded over the GPUs, C rows all-gathered"
 
 # DRAM bytes (read + write) of one 8192^3 launch of the GEMM kernel, measured
 # with ncu (dram__bytes_read.sum + dram__bytes_write.sum of the 3xTF32 launch;
@@ -144,7 +145,7 @@ def run_reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference CPU RNG, U(-1,1))",
-        "config": {"workload": WORKLOAD, "size": n, "mode": "fp32 (reference CPU loop)"},
+        "config": {"workload": workload(n), "size": n, "mode": "fp32 (reference CPU loop)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": used, "kind": kind, "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -419,7 +420,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic U(-1,1) (torch generator, seeded), resident in HBM",
-        "config": {"workload": WORKLOAD, "size": n, "rows_per_gpu": rows,
+        "config": {"workload": workload(n), "size": n, "rows_per_gpu": rows,
                    "mode": args.mode,
                    "parallelism": f"row-shard x{world}" + (GATHER_NAMES[args.gather] if world > 1 else ""),
                    "l2": "inputs larger than L2 (2 x 268 MB operands, 268 MB output)"},
