@@ -412,9 +412,9 @@ def main():
     peak = tf32_peak / 3.0 if args.mode == "3xtf32" else tf32_peak
     per_launch_flops = 2.0 * rows * n * n
     achieved = per_launch_flops / (kern_ms * 1e-3) / 1e12
-    traffic = NCU_TRAFFIC_BYTES_PER_LAUNCH.get(args.mode)
-    if traffic is not None and world > 1:
-        traffic = traffic / world
+    # captured for the one-GPU 8192^3 launch only; a row shard's launch has
+    # its own L2 reuse, so other shapes report none rather than a scaled guess
+    traffic = NCU_TRAFFIC_BYTES_PER_LAUNCH.get(args.mode) if (world == 1 and n == SIZE) else None
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
@@ -423,9 +423,14 @@ def main():
         "config": {"workload": workload(n), "size": n, "rows_per_gpu": rows,
                    "mode": args.mode,
                    "parallelism": f"row-shard x{world}" + (GATHER_NAMES[args.gather] if world > 1 else ""),
-                   "l2": "inputs larger than L2 (2 x 268 MB operands, 268 MB output)"},
+                   "l2": (f"operands 2 x {n * n * 4 / 1e6:.0f} MB, output {n * n * 4 / 1e6:.0f} MB: "
+                          + ("each larger than the 126 MB L2" if n * n * 4 > 126e6
+                             else "smaller than the 126 MB L2 and not flushed (not a contract measurement)"))},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak, "traffic": traffic,
+                     "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one 8192^3 launch "
+                                        "(profiles/dram_mg_gemm_tc_kernel_8192.md)" if traffic is not None
+                                        else "not captured for this shape"),
                      "peak_source": (f"{src} bf16 dense {bf16:.1f} TFLOP/s / 2 = TF32 {tf32_peak:.1f}"
                                      + (" / 3 products per fp32-accurate term" if args.mode == "3xtf32" else "")),
                      "kernel": "mg_gemm_tc_kernel", "kernel_ms": kern_ms},
