@@ -448,6 +448,116 @@ def main():
 
 
 # ------------------------------------------------------------------ small workloads
+SMALL = {
+    "batched": (3 * 2.0 * 8 * 256 * 384 * 384,
+                {"workload": "batched fp32 matmul A[8,256,384] @ W[384,384], backward with dC = ones",
+                 "gemms": "C = A W; dA = dC W^T; dW = A^T dC (batch folded into K = 2048)"}),
+    "linear": (3 * 2.0 * 16384 * 1536 * 384,
+               {"workload": "linear layer X[16384,384] @ W[1536,384]^T + b[1536], backward with dY ~ N(0,1)",
+                "gemms": "Y = X W^T + b (bias fused); dX = dY W; dW = dY^T X (transposed views in place)"}),
+    "attention": (6 * 2.0 * 64 * 6 * 256 * 256 * 64,
+                  {"workload": "causal attention Q, K, V [64,6,256,64]: P = softmax(Q K^T / 8 + causal) fused, "
+                               "O = P V, backward with dO = ones",
+                   "gemms": "P (score product + mask + row softmax in the epilogue), O = P V, "
+                            "dS = P (dP - rowsum(P dP)) with dP = dO V^T (softmax backward in the epilogue), "
+                            "dV = P^T dO, dQ/8 = dS K, dK = dS^T (Q/8): 6 products, 6 launches"}),
+}
+
+
+def small_desc(workload):
+    flops, desc = SMALL[workload]
+    return flops, dict(desc)
+
+
+def run_small_reference(args):
+    """--impl reference for the one-GPU GEMM workloads: the same step through
+    the reference's own CPU Functional::matmul and autograd backward
+    (oracle/_ref, built from the reference sources; the C restatement when that
+    build is absent), on a bounded sample of each step (a slice of its rows or
+    sequences), one core -- the reference's CPU path is single-threaded. GEMM
+    TFLOP/s over the sample, like the GPU arm's GEMM-only rate."""
+    rank, _, _ = env_rank()
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_bridge as ob
+    use_ref = ob.ref_available()
+    kind = "reference" if use_ref else "port"
+
+    def fwd_bwd(A, B, dC, transB=False, bias=None):   # forward + the backward's two GEMMs
+        if use_ref:
+            ob.ref_matmul_backward(A, B, dC, False, transB, bias)
+        else:
+            ob.oracle_matmul(A, B, False, transB, bias)
+            ob.oracle_matmul_backward(A, B, dC, False, transB, None if bias is None else bias.shape)
+
+    mm = ob.ref_matmul if use_ref else ob.oracle_matmul
+    full_flops, desc = small_desc(args.workload)
+    if args.workload == "batched":
+        A, W = ob.seeded_uniform((8, 256, 384), 20), ob.seeded_uniform((384, 384), 21)
+        dC = np.ones((8, 256, 384), np.float32)
+        flops, sample = full_flops, "the whole step"
+
+        def step():
+            t0 = time.perf_counter()
+            fwd_bwd(A, W, dC)
+            return time.perf_counter() - t0
+    elif args.workload == "linear":
+        rows = 1024
+        bound = (6.0 / 384) ** 0.5
+        X = ob.seeded_uniform((rows, 384), 22)
+        W, b = ob.seeded_uniform((1536, 384), 23, -bound, bound), ob.seeded_uniform((1536,), 24, -bound, bound)
+        dY = ob.seeded_normal((rows, 1536), 25)
+        flops, sample = 3 * 2.0 * rows * 1536 * 384, f"{rows} of the 16384 rows of X (and dY)"
+
+        def step():
+            t0 = time.perf_counter()
+            fwd_bwd(X, W, dY, True, b)
+            return time.perf_counter() - t0
+    else:
+        nb = 4
+        Q = ob.seeded_normal((nb, 6, 256, 64), 26, 0.0, 0.125)
+        K = ob.seeded_normal((nb, 6, 256, 64), 27, 0.0, 0.125)
+        V = ob.seeded_normal((nb, 6, 256, 64), 28)
+        dO = np.ones_like(V)
+        Qs = Q * np.float32(0.125)
+        mask = ob.oracle_causal_mask(256)
+        flops = 6 * 2.0 * nb * 6 * 256 * 256 * 64
+        sample = (f"{nb} of the 64 sequences; the Q K^T product that the last forward + backward call "
+                  f"recomputes is subtracted (its time taken from the step's first product)")
+
+        def step():
+            t0 = time.perf_counter()
+            S = mm(Qs, K, False, True, mask)                        # scores + mask
+            t_qk = time.perf_counter() - t0
+            P = ob.ref_softmax_rows(S) if use_ref else ob.oracle_softmax_rows(S)
+            if use_ref:
+                dP, _, _ = ob.ref_matmul_backward(P, V, dO)         # O = P V; dP = dO V^T, dV = P^T dO
+            else:
+                mm(P, V)
+                dP = mm(dO, V, False, True)
+                mm(P, dO, True, False)
+            dS = P * (dP - (P * dP).sum(-1, keepdims=True))         # SoftOp::_backward
+            fwd_bwd(Qs, K, dS, True)                                 # dQ/8, dK, after Q K^T again
+            return time.perf_counter() - t0 - t_qk                  # less the repeated Q K^T
+    vals = []
+    for i in range(max(1, args.warmup) + max(1, args.steps)):
+        dt = step()
+        if i >= max(1, args.warmup):
+            vals.append(flops / dt / 1e12)
+    value = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": f"{args.workload} fwd+bwd GEMM TFLOP/s", "value": value,
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference CPU RNG)",
+        "config": {**desc, "mode": "fp32 (reference CPU loop)", "gflop_per_step": full_flops / 1e9},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": 1, "kind": kind,
+                         "sample": f"{sample}: {flops / 1e9:.2f} GFLOP per step"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+    return 0
+
+
 def run_small_workload(args):
     """One-GPU forward + backward GEMM workloads of the matmul path (the
     parity configurations, timed): every GEMM through the library's public
@@ -455,6 +565,8 @@ def run_small_workload(args):
     (a 512 MB write) between steps; GEMM-only time from events around each
     library call. TFLOP/s against TF32 / 3 (3xTF32) or TF32; the attention
     score product (HBM-bound) also as GB/s against the measured HBM rate."""
+    if args.impl == "reference":
+        return run_small_reference(args)
     import torch
 
     sys.path.insert(0, ROOT)
@@ -486,9 +598,7 @@ def run_small_workload(args):
         A = torch.empty(8, 256, 384, device=dev).uniform_(-1, 1, generator=g)
         W = torch.empty(384, 384, device=dev).uniform_(-1, 1, generator=g)
         dC = torch.ones(8, 256, 384, device=dev)
-        flops = 3 * 2.0 * 8 * 256 * 384 * 384
-        desc = {"workload": "batched fp32 matmul A[8,256,384] @ W[384,384], backward with dC = ones",
-                "gemms": "C = A W; dA = dC W^T; dW = A^T dC (batch folded into K = 2048)"}
+        flops, desc = small_desc("batched")
 
         def step():
             timed(F.matmul, A, W)
@@ -499,9 +609,7 @@ def run_small_workload(args):
         W = torch.empty(1536, 384, device=dev).uniform_(-bound, bound, generator=g)
         b = torch.empty(1536, device=dev).uniform_(-bound, bound, generator=g)
         dY = torch.empty(16384, 1536, device=dev).normal_(0, 1, generator=g)
-        flops = 3 * 2.0 * 16384 * 1536 * 384
-        desc = {"workload": "linear layer X[16384,384] @ W[1536,384]^T + b[1536], backward with dY ~ N(0,1)",
-                "gemms": "Y = X W^T + b (bias fused); dX = dY W; dW = dY^T X (transposed views in place)"}
+        flops, desc = small_desc("linear")
 
         def step():
             timed(F.matmul, X, W, b, False, True)
@@ -512,12 +620,7 @@ def run_small_workload(args):
         V = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 1, generator=g)
         dO = torch.ones(64, 6, 256, 64, device=dev)
         Qs = Q * 0.125
-        flops = 6 * 2.0 * 64 * 6 * 256 * 256 * 64
-        desc = {"workload": "causal attention Q, K, V [64,6,256,64]: P = softmax(Q K^T / 8 + causal) fused, "
-                            "O = P V, backward with dO = ones",
-                "gemms": "P (score product + mask + row softmax in the epilogue), O = P V, "
-                         "dS = P (dP - rowsum(P dP)) with dP = dO V^T (softmax backward in the epilogue), "
-                         "dV = P^T dO, dQ/8 = dS K, dK = dS^T (Q/8): 6 products, 6 launches"}
+        flops, desc = small_desc("attention")
 
         def step():
             P = timed(F.attention_scores, Q, K, 0.125, True)

@@ -237,6 +237,15 @@ def ref_matmul_backward(A, B, dC, transA=False, transB=False, bias=None):
     return dA, dB, db
 
 
+def ref_softmax_rows(x):
+    """Tensor::softmax(-1) through the reference's own compiled CPU code."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    n = x.shape[-1]
+    ref().ref_softmax_lastdim(_ptr(out), _ptr(x), x.size // n if n else 0, n)
+    return out
+
+
 # ------------------------------------------------------------------ metrics
 def frob_rel_err(x, ref):
     """||x - ref||_F / ||ref||_F in float64 (the Frobenius-normalised error the

@@ -1,10 +1,13 @@
-"""bench.py's reference arm on the host cores: one JSON line with the keys
+"""bench.py's reference arms on the host cores: one JSON line with the keys
 the benchmark contract names (run small here; the driver runs it at 8192),
-and nothing from ranks other than 0."""
+nothing from ranks other than 0, and for the one-GPU workloads the
+reference's own CPU matmul rather than the GPU library."""
 import json
 import os
 import subprocess
 import sys
+
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -34,3 +37,16 @@ def test_reference_arm_prints_one_contract_line():
 def test_reference_arm_other_ranks_stay_silent():
     out = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}, "--size", "256", "--steps", "1")
     assert out.returncode == 0 and out.stdout.strip() == ""
+
+
+
+@pytest.mark.parametrize("workload", ["batched", "linear", "attention"])
+def test_small_workload_reference_arms(workload):
+    """The one-GPU workloads' reference arm times the reference's own CPU
+    matmul and backward on a sample of the step, never the GPU library."""
+    out = _run({}, "--workload", workload, "--steps", "1", "--warmup", "1")
+    assert out.returncode == 0, out.stderr
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    assert d["impl"] == "reference" and d["metric"] == f"{workload} fwd+bwd GEMM TFLOP/s" and d["value"] > 0
+    assert d["cpu_baseline"]["cores"] == 1 and d["cpu_baseline"]["kind"] in ("reference", "port")
+    assert d["e2e"]["h2d_bytes_per_step"] == 0
