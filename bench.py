@@ -469,16 +469,13 @@ def small_desc(workload):
     return flops, dict(desc)
 
 
-def run_small_reference(args):
-    """--impl reference for the one-GPU GEMM workloads: the same step through
-    the reference's own CPU Functional::matmul and autograd backward
-    (oracle/_ref, built from the reference sources; the C restatement when that
-    build is absent), on a bounded sample of each step (a slice of its rows or
-    sequences), one core -- the reference's CPU path is single-threaded. GEMM
-    TFLOP/s over the sample, like the GPU arm's GEMM-only rate."""
-    rank, _, _ = env_rank()
-    if rank != 0:
-        return 0
+def small_reference_rate(workload, steps, warmup):
+    """A one-GPU workload's step through the reference's own CPU
+    Functional::matmul and autograd backward (oracle/_ref, built from the
+    reference sources; the C restatement when that build is absent), on a
+    bounded sample of the step (a slice of its rows or sequences), one core --
+    the reference's CPU path is single-threaded. Returns the cpu_baseline
+    record: GEMM TFLOP/s over the sample (median of `steps` after `warmup`)."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     import oracle_bridge as ob
     use_ref = ob.ref_available()
@@ -492,17 +489,16 @@ def run_small_reference(args):
             ob.oracle_matmul_backward(A, B, dC, False, transB, None if bias is None else bias.shape)
 
     mm = ob.ref_matmul if use_ref else ob.oracle_matmul
-    full_flops, desc = small_desc(args.workload)
-    if args.workload == "batched":
+    if workload == "batched":
         A, W = ob.seeded_uniform((8, 256, 384), 20), ob.seeded_uniform((384, 384), 21)
         dC = np.ones((8, 256, 384), np.float32)
-        flops, sample = full_flops, "the whole step"
+        flops, sample = SMALL["batched"][0], "the whole step"
 
         def step():
             t0 = time.perf_counter()
             fwd_bwd(A, W, dC)
             return time.perf_counter() - t0
-    elif args.workload == "linear":
+    elif workload == "linear":
         rows = 1024
         bound = (6.0 / 384) ** 0.5
         X = ob.seeded_uniform((rows, 384), 22)
@@ -541,18 +537,28 @@ def run_small_reference(args):
             fwd_bwd(Qs, K, dS, True)                                 # dQ/8, dK, after Q K^T again
             return time.perf_counter() - t0 - t_qk                  # less the repeated Q K^T
     vals = []
-    for i in range(max(1, args.warmup) + max(1, args.steps)):
+    for i in range(max(1, warmup) + max(1, steps)):
         dt = step()
-        if i >= max(1, args.warmup):
+        if i >= max(1, warmup):
             vals.append(flops / dt / 1e12)
-    value = statistics.median(vals)
+    return {"value": statistics.median(vals), "unit": "TFLOP/s", "cores": 1, "kind": kind,
+            "sample": f"{sample}: {flops / 1e9:.2f} GFLOP per step"}
+
+
+def run_small_reference(args):
+    """--impl reference for the one-GPU GEMM workloads (small_reference_rate)."""
+    rank, _, _ = env_rank()
+    if rank != 0:
+        return 0
+    full_flops, desc = small_desc(args.workload)
+    cpu = small_reference_rate(args.workload, args.steps, args.warmup)
+    value = cpu["value"]
     print(json.dumps({
         "impl": "reference", "metric": f"{args.workload} fwd+bwd GEMM TFLOP/s", "value": value,
         "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference CPU RNG)",
         "config": {**desc, "mode": "fp32 (reference CPU loop)", "gflop_per_step": full_flops / 1e9},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": 1, "kind": kind,
-                         "sample": f"{sample}: {flops / 1e9:.2f} GFLOP per step"},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
     return 0
@@ -670,6 +676,7 @@ def run_small_workload(args):
         "gpu_launches": int(launches),
         "clocks": clk,
         "per_call_ms": [statistics.mean(x) for x in zip(*each_ms)],
+        "cpu_baseline": None if args.no_cpu_baseline else small_reference_rate(args.workload, 3, 1),
     }
     if args.workload == "attention":
         sbytes = 4.0 * (2 * 64 * 6 * 256 * 64 + 64 * 6 * 256 * 256)
