@@ -865,7 +865,10 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.plan.full_tiles = gp.total_tiles;   // no K split unless launch_tc plans one
     gp.plan.num_kb = gp.num_kb;
     gp.group_m = tuning_int("MG_GEMM_GROUP_M", 16, 1, 1 << 16);
-    gp.chunk_kb = tuning_int("MG_GEMM_CHUNK_KB", mg::kChunkKb, 1, 64);
+    // any positive value; at least the K-blocks of a tile means no promotion at
+    // all (one accumulator over the whole K: within TF32 mode's tolerance, not
+    // within 3xTF32's -- the MMA's accumulation truncates)
+    gp.chunk_kb = tuning_int("MG_GEMM_CHUNK_KB", mg::kChunkKb, 1, 1 << 20);
     gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);
     gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
     gp.presplit = presplit ? 1 : 0;
