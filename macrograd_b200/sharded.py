@@ -1,8 +1,9 @@
 """Row-sharded GEMM across ranks (one process per GPU).
 
 C = A @ B where the rows of A (and so of C) are split over the ranks and B is
-replicated. Rows of C depend only on the same rows of A, so each rank's GEMM is
-independent -- no collective inside the GEMM. When the caller needs the whole C
+replicated -- or, for a batched product, its batches. Rows of C depend only on
+the same rows of A (batches only on their own operands), so each rank's GEMM
+is independent -- no collective inside the GEMM. When the caller needs the whole C
 on every device, the row blocks are all-gathered (NCCL over NVLink on GPUs,
 gloo on CPU in the tests), or -- the B200 path -- sent by each rank's GEMM into
 every rank's C over NVLink peer mappings while it computes (PeerRows +
@@ -30,7 +31,9 @@ def row_block(rows: int, world: int, rank: int) -> Tuple[int, int]:
 
 
 def gather_rows(full: torch.Tensor, local: torch.Tensor, group=None) -> torch.Tensor:
-    """All-gather the ranks' row blocks of C into `full` (every rank)."""
+    """All-gather the ranks' blocks of C along its first dim into `full` (every
+    rank): row blocks of a 2-D C, or batch blocks of a batched one, split as
+    row_block splits that dim."""
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     rows = full.shape[0]
@@ -129,8 +132,11 @@ def sharded_matmul(A_local: torch.Tensor, B: torch.Tensor, full_out: Optional[to
                    group=None, local_out: Optional[torch.Tensor] = None,
                    matmul: Optional[Callable[..., torch.Tensor]] = None) -> torch.Tensor:
     """This rank's rows of C = A @ B, then (if `full_out` is given) C gathered
-    into `full_out` on every rank. `matmul` defaults to the sm_100a library
-    (functional.matmul); tests pass the oracle on CPU."""
+    into `full_out` on every rank. For a batched product the same call shards
+    the batches instead: A_local holds this rank's batches (row_block over the
+    leading dim), B those batches too or one matrix broadcast to all, and the
+    slices are gathered along the leading dim. `matmul` defaults to the
+    sm_100a library (functional.matmul); tests pass the oracle on CPU."""
     if matmul is None:
         from .functional import matmul as gpu_matmul
 

@@ -1,6 +1,7 @@
-"""Row-sharded GEMM + all-gather across ranks, on CPU with gloo (world size 2
-and 3): every rank must end with the full C equal to the oracle's full product
-(rows are independent, so the sharded result is bit-identical)."""
+"""Row-sharded and batch-sharded GEMM + all-gather across ranks, on CPU with
+gloo (world size 2 and 3): every rank must end with the full C equal to the
+oracle's full product (rows, and the batches of a batched product, are
+independent, so the sharded result is bit-identical)."""
 import os
 import socket
 
@@ -50,17 +51,51 @@ def _worker(rank, world, port, M, K, N, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,M", [(2, 64), (2, 67), (3, 50)])
-def test_row_sharded_matmul_gathers_the_oracle_product(world, M):
+def _batch_worker(rank, world, port, nb, shared_b, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        A = ob.seeded_uniform((nb, 9, 12), 6)
+        B = ob.seeded_uniform((12, 10) if shared_b else (nb, 12, 10), 1006)
+        b0, b1 = row_block(nb, world, rank)            # this rank's batches
+        B_local = B if shared_b else B[b0:b1].copy()
+        full = torch.empty(nb, 9, 10)
+        sharded_matmul(torch.from_numpy(A[b0:b1].copy()), torch.from_numpy(B_local), full_out=full,
+                       matmul=_oracle_matmul)
+        q.put((rank, bool(np.array_equal(full.numpy(), ob.oracle_matmul(A, B)))))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        q.put((rank, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _spawn(target, world, *args):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, 48, 40, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, *args, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=120) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
+    return results
+
+
+@pytest.mark.parametrize("world,nb,shared_b", [(2, 6, False), (2, 5, True), (3, 7, False)])
+def test_batch_sharded_matmul_gathers_the_oracle_product(world, nb, shared_b):
+    """A batched product split by its leading (batch) dim: each rank multiplies
+    its batches (B per batch, or one broadcast B) and the slices are gathered
+    along that dim."""
+    results = _spawn(_batch_worker, world, nb, shared_b)
+    assert all(v is True for v in results.values()), results
+
+
+@pytest.mark.parametrize("world,M", [(2, 64), (2, 67), (3, 50)])
+def test_row_sharded_matmul_gathers_the_oracle_product(world, M):
+    results = _spawn(_worker, world, M, 48, 40)
     assert all(v is True for v in results.values()), results
 
 
