@@ -102,6 +102,22 @@ int ref_softmax_lastdim(float* out, const float* in, int64_t rows, int64_t n)
     return 0;
 }
 
+// The softmax derivative through the reference's autograd: P = softmax(S)
+// over the last dim of a [rows, n] tensor, loss = sum(P * G), so S's gradient
+// is what SoftOp::_backward (tensor_ops.cpp:2056-2059) makes of the upstream G.
+int ref_softmax_backward(float* dS, float* P, const float* S, const float* G, int64_t rows, int64_t n)
+{
+    int32_t s[2] = {int32_t(rows), int32_t(n)};
+    Tensor t = make_tensor(S, s, 2, true);
+    Tensor y = t.softmax(-1);
+    Tensor g = make_tensor(G, s, 2, false);
+    Tensor loss = (y * g).flatten().sum(0);
+    loss.backward();
+    std::memcpy(P, y.internal_data(), size_t(rows * n) * sizeof(float));
+    std::memcpy(dS, t.gradient().internal_data(), size_t(rows * n) * sizeof(float));
+    return 0;
+}
+
 // Functional::causal_mask(L, "cpu").
 int ref_causal_mask(float* out, int32_t L)
 {

@@ -6,8 +6,8 @@ built oracle/_ref/libmgref.so from them:
     python tests/golden/make_golden.py
 
 Every output in the fixture comes from the reference's own compiled CPU code
-(Functional::matmul, its autograd backward, Tensor::softmax,
-Functional::causal_mask, Random + Initialization), called through
+(Functional::matmul, its autograd backward, Tensor::softmax and its
+backward, Functional::causal_mask, Random + Initialization), called through
 oracle/ref_driver.cpp. Inputs come from the reference's CPU random stream. The
 fixture is small (a few tens of KB) and is what pins the oracle restatement
 and the GPU kernels where the reference cannot be built (the GPU box).
@@ -112,6 +112,14 @@ def main():
     out["attn/K"] = K
     out["attn/S"] = S
     out["attn/P"] = P
+
+    # the softmax derivative through the reference's autograd (SoftOp::_backward)
+    # on that masked block, for a seeded upstream gradient
+    G = normal(S.size, 43).reshape(S.shape)
+    P2, dS = ob.ref_softmax_backward(S, G)
+    assert np.array_equal(P2, P)
+    out["softmax_bwd/G"] = G
+    out["softmax_bwd/dS"] = dS
 
     path = os.path.join(HERE, "matmul_golden.npz")
     np.savez_compressed(path, **out)

@@ -70,6 +70,8 @@ def ref():
                                             ctypes.c_int32, _I32P, ctypes.c_int32, _I32P,
                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
         lib.ref_softmax_lastdim.argtypes = [_P, _P, ctypes.c_int64, ctypes.c_int64]
+        lib.ref_softmax_backward.restype = ctypes.c_int
+        lib.ref_softmax_backward.argtypes = [_P, _P, _P, _P, ctypes.c_int64, ctypes.c_int64]
         lib.ref_causal_mask.argtypes = [_P, ctypes.c_int32]
         lib.ref_init_uniform.argtypes = [_P, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
         lib.ref_init_normal.argtypes = [_P, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
@@ -244,6 +246,18 @@ def ref_softmax_rows(x):
     n = x.shape[-1]
     ref().ref_softmax_lastdim(_ptr(out), _ptr(x), x.size // n if n else 0, n)
     return out
+
+
+def ref_softmax_backward(S, G):
+    """P = Tensor::softmax(S, -1) and the gradient of sum(P * G) with respect to
+    S, through the reference's own autograd (SoftOp::_backward)."""
+    S = np.ascontiguousarray(S, np.float32)
+    G = np.ascontiguousarray(G, np.float32)
+    P = np.empty_like(S)
+    dS = np.empty_like(S)
+    n = S.shape[-1]
+    ref().ref_softmax_backward(_ptr(dS), _ptr(P), _ptr(S), _ptr(G), S.size // n, n)
+    return P, dS
 
 
 # ------------------------------------------------------------------ metrics

@@ -300,7 +300,8 @@ def test_attention_head_split_as_strided_views(mode):
 def test_fused_softmax_backward(mode, shape):
     """dS = P * (dP - rowsum(P * dP)), dP = dO V^T, from one launch, against
     the same expression in float64 from the oracle's GEMM inputs (the
-    reference's SoftOp::_backward, tensor_ops.cpp:2056-2059)."""
+    reference's SoftOp::_backward, tensor_ops.cpp:2056-2059; test_oracle.py
+    checks the expression against the reference's own autograd)."""
     set_mode(mode)
     L = shape[-2]
     q = ob.seeded_normal(shape, 871, 0.0, 0.125)

@@ -51,6 +51,34 @@ def test_oracle_mask_and_softmax_vs_golden():
     assert np.array_equal(ob.oracle_softmax_rows(S), GOLDEN["attn/P"])
 
 
+def _softmax_backward_expr(P, G):
+    """The expected values the fused softmax-backward epilogue is tested
+    against: P * (G - rowsum(P * G)) in float64."""
+    P64, G64 = P.astype(np.float64), G.astype(np.float64)
+    return P64 * (G64 - (P64 * G64).sum(-1, keepdims=True))
+
+
+def test_softmax_backward_expression_is_the_references_vs_golden():
+    """On the reference's own softmax derivative (SoftOp::_backward through its
+    autograd, golden) the float64 expression agrees to fp32 rounding, and the
+    masked (-inf) scores get exactly zero gradient in both."""
+    S, P = GOLDEN["attn/S"], GOLDEN["attn/P"]
+    dS = GOLDEN["softmax_bwd/dS"]
+    expr = _softmax_backward_expr(P, GOLDEN["softmax_bwd/G"])
+    assert ob.frob_rel_err(expr.astype(np.float32), dS) <= 1e-6
+    masked = np.isneginf(S)
+    assert masked.any() and np.all(dS[masked] == 0) and np.all(expr[masked] == 0)
+
+
+@pytest.mark.skipif(not ob.ref_available(), reason="reference build oracle/_ref not present")
+def test_softmax_backward_expression_is_the_references_vs_reference_build():
+    S = ob.seeded_normal((3, 40, 256), 44, 0.0, 2.0)
+    S[..., 200:] = np.where(ob.seeded_uniform((3, 40, 56), 45) > 0, -np.inf, S[..., 200:])
+    G = ob.seeded_normal((3, 40, 256), 46)
+    P, dS = ob.ref_softmax_backward(S, G)
+    assert ob.frob_rel_err(_softmax_backward_expr(P, G).astype(np.float32), dS) <= 1e-6
+
+
 # README.md:166-235: least squares A x = y by gradient descent through
 # Functional::matmul (GEMV: B is 1-D) and mean_squared_error; printed losses
 # and final parameters / gradients to 4 decimals.
