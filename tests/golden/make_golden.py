@@ -45,6 +45,8 @@ BACKWARD = [
     ("linear_bias", (12, 8), (6, 8), (6,), False, True, "normal", 32),
     ("attn_like", (2, 3, 8, 4), (2, 3, 8, 4), None, False, True, "normal", 33),
     ("trans_a_bwd", (2, 9, 5), (2, 9, 3), None, True, False, "normal", 34),
+    ("bias_full_bwd", (2, 2, 8, 4), (2, 2, 8, 4), (8, 8), False, True, "normal", 35),
+    ("bias_col_bwd", (3, 7, 5), (5, 9), (7, 1), False, False, "normal", 36),
 ]
 
 
