@@ -33,19 +33,28 @@ from ._lib import MacrogradError, check, i32_array
 
 
 # ------------------------------------------------------------------ shapes
+def _shape_str(shape: Sequence[int]) -> str:
+    """A shape as the reference prints it (Shape::str): "(3, 4)", "(5)"."""
+    return "(" + ", ".join(str(int(x)) for x in shape) + ")"
+
+
 def equalize(a_shape: Sequence[int], b_shape: Sequence[int], transA: bool, transB: bool):
     """Rank-equalised storage shapes and the output shape, with the reference's
-    checks (tensor_ops.cpp:4521-4579). Returns (A, B, out, a_was_1d, b_was_1d)."""
+    checks and their messages (tensor_ops.cpp:4521-4579). Returns (A, B, out,
+    a_was_1d, b_was_1d)."""
     a, b = list(a_shape), list(b_shape)
-    if len(a) == 0 or len(b) == 0:
+    if len(a) == 0:
         raise MacrogradError(_lib.MG_ERR_INVALID,
-                             "Trying to matrix multiply two tensors while a tensor is empty.")
-    if transA and len(a) < 2:
+                             "Trying to matrix multiply two tensors while the first tensor is empty.")
+    if len(b) == 0:
         raise MacrogradError(_lib.MG_ERR_INVALID,
-                             "Addint a transposition to a single dimensional tensor for a matmul call is not allowed.")
-    if transB and len(b) < 2:
-        raise MacrogradError(_lib.MG_ERR_INVALID,
-                             "Addint a transposition to a single dimensional tensor for a matmul call is not allowed.")
+                             "Trying to matrix multiply two tensors while the second tensor is empty.")
+    for flag, t, name in ((transA, a, "transA"), (transB, b, "transB")):
+        if flag and len(t) < 2:
+            raise MacrogradError(_lib.MG_ERR_INVALID,
+                                 "Addint a transposition to a single dimensional tensor for a matmul call is not "
+                                 "allowed.\n"
+                                 f"Make sure your tensor has at least 2 dimensions if you set '{name}' as true.")
     a_was_1d, b_was_1d = len(a) == 1, len(b) == 1
     if a_was_1d:
         a = [1] + a
@@ -60,30 +69,42 @@ def equalize(a_shape: Sequence[int], b_shape: Sequence[int], transA: bool, trans
     if ka != kb:
         raise MacrogradError(_lib.MG_ERR_INVALID,
                              "Incompatible dimensions found inside a matmul() call.\n"
-                             f"Matrix0 shape: {tuple(a_shape)} | Matrix1 shape: {tuple(b_shape)}")
+                             "Please make sure your tensors follow proper matrix multiplication logic "
+                             "(...,M,K) @ (...,K,N) = (...,M,N).\n"
+                             f"Matrix0 shape: {_shape_str(a_shape)} | Matrix1 shape: {_shape_str(b_shape)}")
     for i in range(len(a) - 2):
         if not (a[i] == b[i] or a[i] == 1 or b[i] == 1):
             raise MacrogradError(_lib.MG_ERR_INVALID,
                                  "Trying to matrix multiply two tensors with incompatible shapes.\n"
-                                 f"Found shapes | Unsqueezed Matrix0: {tuple(a)} | Unsqueezed Matrix1: {tuple(b)}")
+                                 "Make sure leading shapes are compatible, meaning they have the same sizes or one "
+                                 "of them is unitary for broadcasting.\n"
+                                 f"Found shapes | Unsqueezed Matrix0: {_shape_str(a)} | "
+                                 f"Unsqueezed Matrix1: {_shape_str(b)}")
     out = [max(x, y) for x, y in zip(a[:-2], b[:-2])]
     out += [a[-1] if transA else a[-2], b[-2] if transB else b[-1]]
     return a, b, out, a_was_1d, b_was_1d
 
 
 def equalize_bias(bias_shape: Sequence[int], out_shape: Sequence[int]):
-    """Bias rank-equalised to the output (tensor_ops.cpp:4784-4785, 4807-4818)."""
+    """Bias rank-equalised to the output, with the reference's checks and
+    messages (tensor_ops.cpp:4784-4785, 4807-4818)."""
     bs = list(bias_shape)
     if len(bs) > len(out_shape):
         raise MacrogradError(_lib.MG_ERR_INVALID,
-                             "Trying to add a bias to a matmul tensor with more dimensions than the matmul output.")
+                             "Trying to add a bias to a matmul tensor with more dimensions than the matmul output.\n"
+                             "Make sure the bias is broadcastable to the matmul output, bias dimensionality must "
+                             "be less or equal.\n"
+                             f"Found shapes | Matmul output: {_shape_str(out_shape)} | Bias: {_shape_str(bs)}")
     while len(bs) < len(out_shape):
         bs = [1] + bs
     for o, x in zip(out_shape, bs):
         if not (o == x or x == 1):
             raise MacrogradError(_lib.MG_ERR_INVALID,
                                  "Trying to add a bias to a matmul tensor with incompatible shapes.\n"
-                                 f"Found shapes | Matmul output: {tuple(out_shape)} | Unsqueezed bias: {tuple(bs)}")
+                                 "Make sure leading shapes are compatible, meaning they have the same sizes or the "
+                                 "bias one is unitary for broadcasting.\n"
+                                 f"Found shapes | Matmul output: {_shape_str(out_shape)} | "
+                                 f"Unsqueezed bias: {_shape_str(bs)}")
     return bs
 
 
@@ -246,8 +267,10 @@ def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = 
     M, K = a.shape[-2], a.shape[-1]
     if b.shape[-2] != K:
         raise MacrogradError(_lib.MG_ERR_INVALID,
-                             f"Incompatible dimensions found inside a matmul() call.\n"
-                             f"Matrix0 shape: {tuple(a.shape)} | Matrix1 shape: {tuple(b.shape)}")
+                             "Incompatible dimensions found inside a matmul() call.\n"
+                             "Please make sure your tensors follow proper matrix multiplication logic "
+                             "(...,M,K) @ (...,K,N) = (...,M,N).\n"
+                             f"Matrix0 shape: {_shape_str(a.shape)} | Matrix1 shape: {_shape_str(b.shape)}")
     N = b.shape[-1]
     nb = max(a.dim(), b.dim()) - 2
     ash = [1] * (nb - (a.dim() - 2)) + list(a.shape[:-2])
@@ -259,7 +282,10 @@ def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = 
         if not (ash[i] == bsh[i] or ash[i] == 1 or bsh[i] == 1):
             raise MacrogradError(_lib.MG_ERR_INVALID,
                                  "Trying to matrix multiply two tensors with incompatible shapes.\n"
-                                 f"Found shapes | Matrix0: {tuple(a.shape)} | Matrix1: {tuple(b.shape)}")
+                                 "Make sure leading shapes are compatible, meaning they have the same sizes or one "
+                                 "of them is unitary for broadcasting.\n"
+                                 f"Found shapes | Unsqueezed Matrix0: {_shape_str(ash + [M, K])} | "
+                                 f"Unsqueezed Matrix1: {_shape_str(bsh + [K, N])}")
         batch.append(max(ash[i], bsh[i]))
     if nb > _lib.MG_MAX_BATCH_DIMS:
         raise MacrogradError(_lib.MG_ERR_UNSUPPORTED, f"more than {_lib.MG_MAX_BATCH_DIMS} leading dims")

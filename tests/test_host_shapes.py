@@ -91,3 +91,52 @@ def test_calls_take_one_device():
         F._one_device(a, torch.zeros(2, device="meta"))
     with pytest.raises(MacrogradError, match="different devices"):
         F._one_device(a, stream=types.SimpleNamespace(device=torch.device("cuda", 0)))
+
+
+# (A shape, B shape, transA, transB, bias shape or None): shape errors of
+# Functional::matmul and its bias form
+ERROR_CASES = [
+    ((3, 4), (5, 6), False, False, None),
+    ((5,), (4, 3), False, False, None),
+    ((4,), (4, 3), True, False, None),
+    ((2, 3), (3,), False, True, None),
+    ((2, 3, 4), (3, 4, 5), False, False, None),
+    ((4, 3), (3, 5), False, False, (7,)),
+    ((2, 4, 3), (3, 5), False, False, (3, 4, 5)),
+    ((4, 3), (3, 5), False, False, (2, 3, 4, 5)),
+]
+
+
+def _our_message(a, b, ta, tb, bias):
+    try:
+        _, _, out, _, _ = F.equalize(a, b, ta, tb)
+        if bias is not None:
+            F.equalize_bias(bias, out)
+    except MacrogradError as e:
+        return str(e).split(": ", 1)[1]
+    return None
+
+
+@pytest.mark.parametrize("case", ERROR_CASES)
+def test_shape_errors_carry_the_references_messages(case):
+    """The reference prints its MACROGRAD_CHECK message and aborts; run it in a
+    child process and compare the message with the one raised here."""
+    import os
+    import subprocess
+    import sys
+
+    import oracle_bridge as ob
+
+    if not ob.ref_available():
+        pytest.skip("reference build oracle/_ref not present")
+    a, b, ta, tb, bias = case
+    bias_src = "None" if bias is None else f"np.zeros({bias}, np.float32)"
+    code = ("import numpy as np, oracle_bridge as ob\n"
+            f"ob.ref_matmul(np.zeros({a}, np.float32), np.zeros({b}, np.float32), {ta}, {tb}, {bias_src})\n")
+    here = os.path.dirname(os.path.abspath(__file__))
+    run = subprocess.run([sys.executable, "-c", code], cwd=here, capture_output=True, text=True, timeout=120)
+    assert run.returncode != 0, "the reference accepted the shapes"
+    text = run.stdout + run.stderr
+    assert "Message: " in text, text
+    ref_message = text.split("Message: ", 1)[1].strip()
+    assert _our_message(a, b, ta, tb, bias) == ref_message
