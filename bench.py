@@ -692,6 +692,30 @@ def run_small_workload(args):
 DECODER_METRIC = "decoder training step tokens/s (6 layers, d_model 384, batch 64 x 256 tokens)"
 
 
+def decoder_reference_rate(T, steps, warmup):
+    """The reference's own CPU training step (its modules, autograd and AdamW
+    through the drop-in build on "cpu") on one of the batch's sequences, one
+    core (the reference's CPU path is single-threaded): the cpu_baseline
+    record, tokens/s, median of `steps` after `warmup`."""
+    from macrograd_b200 import training
+
+    m = training.DecoderStep(device="cpu")
+    try:
+        m.make_batch(5, training.BATCH, T, 0, 1)
+        vals = []
+        for i in range(max(1, warmup) + max(1, steps)):
+            t0 = time.perf_counter()
+            m.forward_backward()
+            m.optimizer_step()
+            dt = time.perf_counter() - t0
+            if i >= max(1, warmup):
+                vals.append(T / dt)
+    finally:
+        m.close()
+    return {"value": statistics.median(vals), "unit": "tokens/s", "cores": 1, "kind": "reference",
+            "sample": f"1 sequence of {T} tokens per step (full model, forward + backward + AdamW), 1 core"}
+
+
 def run_decoder(args):
     """The decoder-only character model's training step (6 layers, 6 heads,
     d_model 384, MLP 1536, context 256, vocab 65, batch 64), built from the
@@ -712,26 +736,14 @@ def run_decoder(args):
         # the reference's own CPU step on one of its sequences (it is single-threaded)
         if rank != 0:
             return 0
-        m = training.DecoderStep(device="cpu")
-        m.make_batch(5, training.BATCH, T, 0, 1)
-        vals = []
-        for i in range(max(1, args.warmup) + max(1, args.steps)):
-            t0 = time.perf_counter()
-            m.forward_backward()
-            m.optimizer_step()
-            dt = time.perf_counter() - t0
-            if i >= max(1, args.warmup):
-                vals.append(T / dt)
-        m.close()
-        v = statistics.median(vals)
-        sample = f"1 sequence of {T} tokens per step (full model, forward + backward + AdamW), 1 core"
+        cpu = decoder_reference_rate(T, args.steps, args.warmup)
+        v = cpu["value"]
         print(json.dumps({"impl": "reference", "metric": DECODER_METRIC, "value": v, "unit": "tokens/s",
                           "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                           "data": "synthetic token ids (reference CPU RNG)",
                           "config": {"workload": "decoder training step", **cfg, "batch": training.BATCH},
-                          "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
-                                           "sample": sample},
+                          "cpu_baseline": cpu,
                           "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                                   "d2h_bytes_per_step": 0}}), flush=True)
         return 0
@@ -739,6 +751,8 @@ def run_decoder(args):
     import torch
     import torch.distributed as dist
 
+    # the reference's CPU step, timed before any CUDA work (rank 0 of a one-GPU run)
+    cpu = decoder_reference_rate(T, 1, 1) if (world == 1 and not args.no_cpu_baseline) else None
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
@@ -822,6 +836,7 @@ def run_decoder(args):
         "loss": losses[-1] if losses else None,
         "gpu_launches": int(launches),
         "clocks": clk,
+        "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
     return 0
