@@ -50,3 +50,17 @@ def test_small_workload_reference_arms(workload):
     assert d["impl"] == "reference" and d["metric"] == f"{workload} fwd+bwd GEMM TFLOP/s" and d["value"] > 0
     assert d["cpu_baseline"]["cores"] == 1 and d["cpu_baseline"]["kind"] in ("reference", "port")
     assert d["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_decoder_reference_arm():
+    """The decoder workload's reference arm: the reference's own CPU training
+    step (drop-in build on "cpu") on one sequence, as tokens/s."""
+    from macrograd_b200 import training
+
+    if not os.path.exists(training.SEAM):
+        pytest.skip("drop-in build not available (needs the reference sources at build time)")
+    out = _run({}, "--workload", "decoder", "--steps", "1", "--warmup", "1")
+    assert out.returncode == 0, out.stderr
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    assert d["impl"] == "reference" and d["unit"] == "tokens/s" and d["value"] > 0
+    assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] == 1
