@@ -172,7 +172,8 @@ void oracle_reduce_to(float* dst, const float* src, const int32_t* dst_shape,
     /* Reduce src over every dim where dst is 1 and src is not, in increasing dim
      * order (tensor_ops.cpp:3394-3398), then add elementwise with broadcast of
      * the remaining unit dims of src. */
-    int32_t cur_shape[16];
+    int32_t cur_shape[16] = {0};
+    if (rank < 0 || rank > 16) return;
     int64_t n = 1;
     for (int32_t i = 0; i < rank; i++) { cur_shape[i] = src_shape[i]; n *= src_shape[i]; }
     float* cur = (float*)malloc((size_t)(n > 0 ? n : 1) * sizeof(float));
