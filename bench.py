@@ -19,7 +19,6 @@ Prints one JSON line on rank 0.
 from __future__ import annotations
 
 import argparse
-import ctypes
 import json
 import os
 import statistics

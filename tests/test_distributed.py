@@ -12,7 +12,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle_bridge as ob
-from macrograd_b200.sharded import gather_rows, row_block, sharded_matmul
+from macrograd_b200.sharded import row_block, sharded_matmul
 
 
 def _free_port():
