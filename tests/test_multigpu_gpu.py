@@ -7,8 +7,9 @@ with the K split forced (MG_GEMM_SPLIT_MIN_KB=1) the last split level's rows
 go out through every CTA's export warps; a 1001-wide C takes the 4-byte copy
 paths. The NCCL gather of the same kernel's rows must be bit-identical. The
 copy-engine form (MG_GEMM_EXPORT=2: the GEMM in column bands, each band
-copied to the peer by cudaMemcpy2DAsync; forced to 256-column bands here, so
-that a 1024- or 1001-wide C makes four) may split bands along K where one
+copied to the peer by cudaMemcpy2DAsync; once forced to 256-column bands, so
+that a 1024- or 1001-wide C makes four, once in the planner's tapering bands)
+may split bands along K where one
 launch does not, so its C is compared bit for bit with every rank's own rows
 broadcast over NCCL instead. Skipped when fewer than 2 GPUs are visible."""
 import os
@@ -62,7 +63,12 @@ def _worker(rank, world, port, n, q):
             lib.mg_set_mode(mode)
             os.environ["MG_GEMM_EXPORT"] = export
             os.environ["MG_GEMM_SPLIT_MIN_KB"] = min_kb
-            os.environ["MG_GEMM_BAND_COLS"] = "1"    # bands of one 256-wide column: several copies
+            # copy engines: one case in bands of one 256-wide column, the other in the
+            # planner's own tapering bands (two of two columns here, K split to 1 K-block)
+            if export == "2" and min_kb == "1":
+                os.environ.pop("MG_GEMM_BAND_COLS", None)
+            else:
+                os.environ["MG_GEMM_BAND_COLS"] = "1"
             full = torch.full((n, n), float("nan"), device=dev)
             peers = PeerRows(full)
             for _ in range(2):                       # two calls in a row into the same buffers
