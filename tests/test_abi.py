@@ -45,11 +45,11 @@ def test_every_declared_symbol_is_exported():
     assert declared == set(_lib.SIGNATURES), "ctypes binding out of sync with the header"
 
 
-def test_kernel_image_is_sm100a():
-    out = subprocess.run(["cuobjdump", "--list-elf", _lib.lib_path()], capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    assert "sm_100a" in out.stdout
+def test_kernels_are_built_for_sm100a_only():
+    """The build compiles every kernel for sm_100a and nothing else."""
+    from macrograd_b200 import build
+
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def test_desc_init_defaults():
