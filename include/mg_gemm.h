@@ -67,7 +67,10 @@ enum {
  * op(A) is A stored [M][K] with row stride lda (trans_a = 0) or stored [K][M]
  * (trans_a = 1); op(B) is B stored [K][N] (trans_b = 0) or [N][K] (trans_b = 1).
  * The batch index b runs over batch[0..batch_rank) (row-major); an operand's
- * stride 0 on a dim broadcasts it there. Operands are fp32 device memory. */
+ * stride 0 on a dim broadcasts it there. C's stride 0 on a dim of size > 1
+ * makes it a reduction dim: C receives the product summed over it (not with
+ * the softmax epilogues; a bias must not vary along it). Operands are fp32
+ * device memory. */
 typedef struct mg_gemm_desc {
     int32_t M, N, K;
     int32_t trans_a, trans_b;
@@ -112,6 +115,34 @@ mg_status mg_matmul_bias(float* out, const float* A, const float* B, const float
                          const int32_t* out_shape, const int32_t* A_shape,
                          const int32_t* B_shape, const int32_t* bias_shape,
                          int32_t rank, int32_t trans_a, int32_t trans_b, void* stream);
+
+/* Replaces the gradient accumulation of MatMulOp / MatMulBiasOp::_backward
+ * (tensor_ops.cpp:4504-4517, :4723-4737):
+ *     grad += Functional::matmul(X, Y, tX, tY)
+ * which the reference runs as kernel_ops::matmul into a zero-filled
+ * temporary followed by kernel_ops::shaped_add (cuda_backend.cu:4496-4592;
+ * its squeeze kernel when the gradient's operand was broadcast). Here it is
+ * one GEMM: out = beta * out + sum over the broadcast dims of op(A) op(B).
+ * Shapes as mg_matmul, except that out_shape may be 1 on a leading dim where
+ * max(A_i, B_i) is not: the product is summed over that dim (folded into the
+ * kernel's K loop, no temporary). beta is 0 (overwrite) or 1 (accumulate into
+ * out, the `+=`). */
+mg_status mg_matmul_accumulate(float* out, const float* A, const float* B,
+                               const int32_t* out_shape, const int32_t* A_shape,
+                               const int32_t* B_shape, int32_t rank, int32_t trans_a,
+                               int32_t trans_b, float beta, void* stream);
+
+/* Replaces the squeeze direction of kernel_ops::shaped_add
+ * (cuda_backend.cu:4496-4592) behind `tensor += other` when the tensor
+ * broadcasts to `other` (tensor_ops.cpp:3393-3446), e.g. the bias gradient of
+ * MatMulBiasOp::_backward (`bias.internal_gradient() += out.gradient()`,
+ * tensor_ops.cpp:4736):
+ *     dst = beta * dst + src summed over the dims where dst_shape is 1.
+ * Both shapes have `rank` dims; dst_shape[i] is src_shape[i] or 1; both
+ * tensors contiguous fp32. beta is 0 or 1. Deterministic (fixed summation
+ * order for given shapes and device). */
+mg_status mg_sum_into(float* dst, const float* src, const int32_t* dst_shape,
+                      const int32_t* src_shape, int32_t rank, float beta, void* stream);
 
 /* Fused attention-score product: out = softmax_rows(alpha * op(A) op(B) (+ bias)
  * (+ causal mask)), i.e. what the reference's MultiHeadSelfAttention computes
@@ -175,22 +206,32 @@ mg_status mg_ipc_close(void* dev_ptr);
  * Some callers cannot let a library allocate device memory during a call:
  * runtimes that plan all device memory ahead of time and own every byte of
  * it, or latency-critical loops that must not touch an allocator. mg_matmul
- * itself allocates only in one case -- an operand whose row pitch is not a
- * multiple of 16 bytes (e.g. rows of 65 floats) is first copied into padded
- * scratch -- and this entry point takes that scratch from a fixed buffer
- * inside the library instead: a file-scope device array of
- * MG_NOALLOC_SCRATCH_BYTES, which every GPU that loads the library holds
- * until the process exits. It calls no cudaMalloc / cudaFree and no
- * allocator. Arguments, results and errors are those of mg_matmul.
+ * takes scratch memory (through mg_set_allocator's allocator, else the
+ * library's own stream-ordered pool) in three cases:
+ *   1. an operand whose row pitch is not a multiple of 16 bytes (e.g. rows of
+ *      65 floats) is first copied into padded scratch;
+ *   2. when the last wave of output tiles would leave SMs idle, it is split
+ *      along K, and the partial ranges exchange fp32 partial tiles through
+ *      scratch slots with a zeroed counter per slot;
+ *   3. only with MG_GEMM_PRESPLIT=1: the 3xTF32 lo planes of both operands.
+ * This entry point takes 1 and 2 from a fixed buffer inside the library
+ * instead -- a file-scope device array of MG_NOALLOC_SCRATCH_BYTES, which
+ * every GPU that loads the library holds until the process exits -- and never
+ * does 3. It calls no cudaMalloc / cudaFree and no allocator. Arguments,
+ * results and errors are those of mg_matmul.
  *
- * Limits: a call whose re-laid-out operands would need more than
+ * Limits: a call whose re-laid-out operands (case 1) would need more than
  * MG_NOALLOC_SCRATCH_BYTES is rejected with MG_ERR_INVALID before anything
- * runs. The buffer is shared by all calls on a device and keeps the previous
- * call's contents (every byte a call reads it has written first, so nothing
- * needs clearing); calls that overlap on the GPU (several streams, or several
- * host threads) race on it, so serialise them. The first call on each device
- * looks up the buffer's device address; make that first call before any
- * stream capture. */
+ * runs. When the K-split slots (case 2) do not fit in what case 1 leaves of
+ * the buffer, the call runs without the K split: same result within the
+ * tolerance, possibly slower than mg_matmul. The buffer is shared by all
+ * calls on a device and keeps the previous call's contents (the split
+ * counters are cleared on the call's stream before the kernel runs; every
+ * other byte a call reads it has written first); calls that overlap on the
+ * GPU (several streams, or several host threads) race on it, so serialise
+ * them. The first call on each device looks up the buffer's device address;
+ * make that first call before any stream capture. The cached address is not
+ * valid across cudaDeviceReset. */
 #define MG_NOALLOC_SCRATCH_BYTES (16u << 20)
 mg_status mg_matmul_noalloc(float* out, const float* A, const float* B,
                             const int32_t* out_shape, const int32_t* A_shape,
@@ -199,8 +240,10 @@ mg_status mg_matmul_noalloc(float* out, const float* A, const float* B,
 
 /* Workspace allocator, stream-ordered like the reference's MemPool
  * (cuda_backend.h:63-79: cudaMallocAsync / cudaFreeAsync on the library
- * stream). The library asks for scratch only on paths that need it (operands
- * whose row stride is not a multiple of 16 bytes are re-laid out there).
+ * stream). The library asks for scratch only on paths that need it: operands
+ * whose row stride is not a multiple of 16 bytes are re-laid out there, a
+ * K-split last wave exchanges its partial tiles there, and MG_GEMM_PRESPLIT=1
+ * keeps the 3xTF32 lo planes there.
  * Passing NULL functions restores the default (cudaMallocAsync on the call's
  * stream). The allocator replaces MemPool::allocate/free for the workspace. */
 typedef void* (*mg_alloc_fn)(size_t bytes, void* stream, void* ctx);

@@ -80,6 +80,9 @@ SIGNATURES = {
     "mg_gemm": (ctypes.c_int, [ctypes.POINTER(GemmDesc), _P, _P, _P, _P, _P]),
     "mg_matmul": (ctypes.c_int, [_P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
     "mg_matmul_bias": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32P, _I32, _I32, _I32, _P]),
+    "mg_matmul_accumulate": (ctypes.c_int, [_P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32, ctypes.c_float,
+                                            _P]),
+    "mg_sum_into": (ctypes.c_int, [_P, _P, _I32P, _I32P, _I32, ctypes.c_float, _P]),
     "mg_matmul_softmax": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32P, _I32, _I32, _I32,
                                          ctypes.c_float, _I32, _P]),
     "mg_matmul_softmax_backward": (ctypes.c_int, [_P, _P, _P, _P, _I32P, _I32P, _I32P, _I32, _I32, _I32,

@@ -18,6 +18,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "mg_gemm.h"
 #include "mg_gemm_kernel.cuh"
@@ -35,19 +36,23 @@ std::mutex g_mu;
 
 __device__ int g_device_status[2];
 
+constexpr int kMaxDevices = 64;
+
 // Fixed scratch of mg_matmul_noalloc (MG_NOALLOC_SCRATCH_BYTES), one copy per
 // GPU that loads this library, held until the process exits. In host code this
-// name is only a handle for cudaGetSymbolAddress, never a device address.
+// name is only a handle for cudaGetSymbolAddress, never a device address. It
+// holds the padded copies of operands TMA cannot read in place and, after
+// them, the K-split partial slots and their counters.
 static __device__ __align__(256) uint8_t g_noalloc_scratch[MG_NOALLOC_SCRATCH_BYTES];
-std::atomic<uint8_t*> g_noalloc_ptr[64];   // its device address, per device ordinal (null: not yet)
-
-constexpr int kMaxDevices = 64;
+// its device address, per device ordinal (null: not looked up yet; not valid
+// across cudaDeviceReset, like the rest of the per-device state)
+std::atomic<uint8_t*> g_noalloc_ptr[kMaxDevices];
 struct DeviceState {
     std::atomic<bool> ready{false};   // set last, under g_mu (read without it)
     int sm_count = 0;
     int max_smem = 0;
-    size_t attr_smem[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // dynamic smem opted in, per kernel variant
-    int max_clusters[4] = {0, 0, 0, 0};               // resident CTA pairs, per pair-kernel tile width
+    size_t attr_smem[3][8] = {};      // dynamic smem opted in, per kernel variant [row epilogue][width, pair]
+    int max_clusters[3][4] = {};      // resident CTA pairs, per pair-kernel [row epilogue][tile width]
     int* status = nullptr;   // device address of g_device_status
     cudaMemPool_t pool = nullptr;   // the library's own stream-ordered pool (workspace)
     // the copy-engine all-gather: a stream per destination, an event per band
@@ -113,10 +118,10 @@ int32_t resolve_default_mode()
     return g_mode.load();
 }
 
-template <int BN, bool kPair>
+template <int BN, bool kPair, int kRow>
 constexpr auto kernel_of()
 {
-    return &mg::mg_gemm_tc_kernel<BN, kPair>;
+    return &mg::mg_gemm_tc_kernel<BN, kPair, kRow>;
 }
 
 int bn_slot(int bn) { return bn == 64 ? 0 : (bn == 128 ? 1 : (bn == 224 ? 3 : 2)); }
@@ -364,6 +369,92 @@ __global__ void k0_fill_kernel(FillParams p)
     }
 }
 
+// dst = beta * dst + src summed over the dims where dst has size 1 and src
+// does not: the squeeze direction of the reference's `+=` (its
+// kernel_ops::shaped_add, cuda_backend.cu:4496-4592, reached from
+// tensor_ops.cpp:3393-3446), e.g. a bias gradient, the output gradient summed
+// over its rows. Dims are canonicalised on the host (size-1 dims dropped,
+// neighbours of the same kind merged): src is then nk kept dims and nr reduced
+// dims, interleaved, contiguous. Deterministic: the reduced range is cut into
+// `splits` contiguous parts, each part's partial sums go to part[split][o],
+// and sum_parts_kernel adds them in split order.
+struct SumParams {
+    const float* src;
+    float* dst;
+    float* part;                // [splits][P] partial sums (splits > 1)
+    int64_t P, R;               // output elements; reduced elements per output
+    int64_t rchunk;             // reduced elements per split
+    int splits;
+    int rows;                   // src is [R][P] row-major (the common case)
+    int vec;                    // rows && P % 4 == 0 and 16-byte aligned pointers: float4 columns
+    float beta;
+    int nk, nr;
+    int64_t ksize[MG_MAX_BATCH_DIMS + 2], kstride[MG_MAX_BATCH_DIMS + 2];   // kept dims, outer first
+    int64_t rsize[MG_MAX_BATCH_DIMS + 2], rstride[MG_MAX_BATCH_DIMS + 2];   // reduced dims, outer first
+};
+
+__device__ __forceinline__ int64_t sum_src_offset(const SumParams& p, int64_t o, int64_t r)
+{
+    int64_t off = 0;
+    for (int i = p.nk - 1; i >= 0; --i) {
+        off += (o % p.ksize[i]) * p.kstride[i];
+        o /= p.ksize[i];
+    }
+    for (int i = p.nr - 1; i >= 0; --i) {
+        off += (r % p.rsize[i]) * p.rstride[i];
+        r /= p.rsize[i];
+    }
+    return off;
+}
+
+__global__ void sum_into_kernel(SumParams p)
+{
+    const int s = blockIdx.y;
+    const int64_t r0 = (int64_t)s * p.rchunk;
+    const int64_t r1 = min(p.R, r0 + p.rchunk);
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (p.vec) {
+        // four consecutive outputs per thread, rows read as float4 (coalesced)
+        if (t >= p.P / 4) return;
+        const float4* src = reinterpret_cast<const float4*>(p.src) + t;
+        const int64_t ld = p.P / 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int64_t r = r0; r < r1; ++r) {
+            const float4 v = __ldg(src + r * ld);
+            acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+        }
+        if (p.splits > 1) {
+            reinterpret_cast<float4*>(p.part + (int64_t)s * p.P)[t] = acc;
+        } else {
+            float4* d = reinterpret_cast<float4*>(p.dst) + t;
+            if (p.beta != 0.f) {
+                const float4 o = *d;
+                acc.x += p.beta * o.x, acc.y += p.beta * o.y, acc.z += p.beta * o.z, acc.w += p.beta * o.w;
+            }
+            *d = acc;
+        }
+        return;
+    }
+    if (t >= p.P) return;
+    float acc = 0.f;
+    if (p.rows) {
+        for (int64_t r = r0; r < r1; ++r) acc += __ldg(p.src + r * p.P + t);
+    } else {
+        for (int64_t r = r0; r < r1; ++r) acc += __ldg(p.src + sum_src_offset(p, t, r));
+    }
+    if (p.splits > 1) p.part[(int64_t)s * p.P + t] = acc;
+    else p.dst[t] = p.beta != 0.f ? acc + p.beta * p.dst[t] : acc;
+}
+
+__global__ void sum_parts_kernel(const float* __restrict__ part, float* dst, int64_t P, int splits, float beta)
+{
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= P) return;
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) acc += part[(int64_t)s * P + t];
+    dst[t] = beta != 0.f ? acc + beta * dst[t] : acc;
+}
+
 // ---------------------------------------------------------------- workspace
 // Per-call scratch. By default it allocates through the registered allocator
 // (or cudaMallocAsync) and frees stream-ordered at the end of the call. Given
@@ -496,7 +587,7 @@ bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, 
     return true;
 }
 
-template <int BN, bool kPair>
+template <int BN, bool kPair, int kRow>
 mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& malo,
                     const CUtensorMap& mblo, mg::GemmParams& gp, const mg::PeerMaps& pm, cudaStream_t st,
                     Workspace* ws, bool allow_split)
@@ -511,11 +602,11 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
     gp.stages = stages;
     const size_t smem = fixed + per_stage * stages;
-    auto k = kernel_of<BN, kPair>();
+    auto k = kernel_of<BN, kPair, kRow>();
     const int slot = bn_slot(BN) + (kPair ? 4 : 0);
-    if (dev->attr_smem[slot] < smem) {
+    if (dev->attr_smem[kRow][slot] < smem) {
         MG_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        dev->attr_smem[slot] = smem;
+        dev->attr_smem[kRow][slot] = smem;
     }
     if (kPair) {
         // one cluster of two CTAs (two SMs) per work unit, persistent over the
@@ -531,13 +622,13 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (dev->max_clusters[slot - 4] == 0) {
+        if (dev->max_clusters[kRow][slot - 4] == 0) {
             cfg.gridDim = dim3((unsigned)dev->sm_count, 1, 1);
             int n = 0;
             MG_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, k, &cfg));
-            dev->max_clusters[slot - 4] = std::max(1, std::min(n, dev->sm_count / 2));
+            dev->max_clusters[kRow][slot - 4] = std::max(1, std::min(n, dev->sm_count / 2));
         }
-        const int resident = dev->max_clusters[slot - 4];
+        const int resident = dev->max_clusters[kRow][slot - 4];
         const bool split_k = setup_split<BN>(gp, resident, ws, st, allow_split);
         gp.dbuf = (!split_k && gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
         if (split_k) {
@@ -639,7 +730,9 @@ int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, const DeviceStat
     const int forced = tuning_int("MG_GEMM_BN", 0, 64, 256);
     const bool row_epi = (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) != 0;
     const bool fits = !row_epi || d->N <= forced;   // softmax: one tile per row
-    if (fits && (forced == 64 || forced == 128 || forced == 256 || (forced == 224 && pair))) return forced;
+    // (the row epilogues are built for widths 64, 128 and 256 only)
+    if (fits && (forced == 64 || forced == 128 || forced == 256 || (forced == 224 && pair && !row_epi)))
+        return forced;
     const int base = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
     if (!pair || base != 256 || row_epi) return base;
     const int64_t m_tiles = (d->M + 2 * mg::kBM - 1) / (2 * mg::kBM);
@@ -716,9 +809,6 @@ void mg_gemm_desc_init(mg_gemm_desc* d, int32_t M, int32_t N, int32_t K, int32_t
     d->mode = MG_MODE_DEFAULT;
 }
 
-// The body of mg_gemm. With arena == nullptr the per-call scratch (operand
-// re-layout) is allocated as usual; with an arena it comes from that fixed
-// buffer and a request that does not fit is rejected before anything runs.
 // Destinations of a row-sharded GEMM whose rows go to every rank's full C.
 struct ScatterSpec {
     int npeers;
@@ -727,6 +817,11 @@ struct ScatterSpec {
     float* peers[mg::kMaxPeers];
 };
 
+// The body of mg_gemm. With arena == nullptr the per-call scratch (operand
+// re-layout, K-split slots, pre-split lo planes) is allocated as usual; with
+// an arena the re-layout and the split slots come from that fixed buffer (a
+// re-layout that does not fit is rejected before anything runs; split slots
+// that do not fit leave the launch unsplit) and there is no pre-split.
 static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, const float* B,
                            const float* bias, void* stream, uint8_t* arena, size_t arena_cap,
                            const ScatterSpec* scatter = nullptr, const float* aux = nullptr)
@@ -737,9 +832,27 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     if ((d->epilogue & mg::kEpiSoftmaxBwd) && !aux)
         return fail(MG_ERR_INVALID, "the softmax-backward epilogue needs P (mg_matmul_softmax_backward)");
     cudaStream_t st = (cudaStream_t)stream;
-    int64_t nbatch = 1;
-    for (int i = 0; i < d->batch_rank; ++i) nbatch *= d->batch[i];
-    if (d->M == 0 || d->N == 0 || nbatch == 0) return MG_OK;
+    // Batch dims where C has stride 0 (and size > 1) are reduction dims: C
+    // receives the sum of the product over them (the `+=` of a gradient whose
+    // operand was broadcast), folded into the kernel's K loop. The others are
+    // tiled; nbatch counts their output matrices.
+    int64_t nbatch = 1, red_steps = 1, all_batch = 1;
+    bool red[MG_MAX_BATCH_DIMS] = {false, false, false, false, false, false};
+    for (int i = 0; i < d->batch_rank; ++i) {
+        all_batch *= d->batch[i];
+        red[i] = d->c_batch_stride[i] == 0 && d->batch[i] > 1;
+        if (red[i]) red_steps *= d->batch[i];
+        else nbatch *= d->batch[i];
+    }
+    if (d->M == 0 || d->N == 0 || all_batch == 0) return MG_OK;
+    if (red_steps > 1) {
+        if (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd))
+            return fail(MG_ERR_INVALID, "a row softmax epilogue cannot reduce over batch dims (C batch stride 0)");
+        if (scatter) return fail(MG_ERR_INVALID, "the scattering GEMM cannot reduce over batch dims");
+        for (int i = 0; i < d->batch_rank; ++i)
+            if (red[i] && (d->epilogue & MG_EPI_BIAS) && d->bias_batch_stride[i] != 0)
+                return fail(MG_ERR_INVALID, "bias varies along reduced batch dim %d", i);
+    }
 
     DeviceState* dev = nullptr;
     s = device_state(&dev);
@@ -755,7 +868,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
         fp.N = d->N;
         fp.nbd = nbd;
         for (int i = 0; i < nbd; ++i) {
-            fp.bsize[i] = d->batch[i];
+            fp.bsize[i] = red[i] ? 1 : d->batch[i];   // a sum over an empty K is 0: C = bias (+ beta C) once
             fp.c_bs[i] = d->c_batch_stride[i];
             fp.bias_bs[i] = d->bias_batch_stride[i];
         }
@@ -831,7 +944,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const int64_t m_tiles_est = (d->M + tile_rows - 1) / tile_rows;
     const int64_t n_tiles_est = (d->N + bn - 1) / bn;
     const bool presplit = mode == MG_MODE_TF32X3 && arena == nullptr &&
-                          want_presplit(2.0 * d->M * d->N * d->K * (double)nbatch, m_tiles_est, n_tiles_est);
+                          want_presplit(2.0 * d->M * d->N * d->K * (double)all_batch, m_tiles_est, n_tiles_est);
     CUtensorMap malo = ma, mblo = mb;
     if (presplit) {
         for (int which = 0; which < 2; ++which) {
@@ -855,7 +968,11 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.M = d->M;
     gp.N = d->N;
     gp.K = d->K;
-    gp.num_kb = (d->K + mg::kBK - 1) / mg::kBK;
+    gp.kb_per = (d->K + mg::kBK - 1) / mg::kBK;
+    if ((int64_t)gp.kb_per * red_steps >= (1ll << 31))
+        return fail(MG_ERR_UNSUPPORTED, "K x reduced batch too large (%lld K-blocks)", (long long)gp.kb_per * red_steps);
+    gp.red_steps = (int)red_steps;
+    gp.num_kb = gp.kb_per * gp.red_steps;
     gp.m_tiles = (d->M + tile_rows - 1) / tile_rows;
     gp.n_tiles = (d->N + bn - 1) / bn;
     gp.tiles_per_batch = gp.m_tiles * gp.n_tiles;
@@ -881,7 +998,8 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
                ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(tile_rows >> 4) << 24);
     gp.nbd = nbd;
     for (int i = 0; i < mg::kMaxBatchDims; ++i) {
-        gp.bsize[i] = i < nbd ? d->batch[i] : 1;
+        gp.bsize[i] = i < nbd && !red[i] ? d->batch[i] : 1;
+        gp.rsize[i] = i < nbd && red[i] ? d->batch[i] : 1;
         gp.a_map[i] = am.map[i];
         gp.b_map[i] = bmp.map[i];
         gp.a_mult[i] = am.mult[i];
@@ -949,20 +1067,34 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     }
 
     // the row softmax (and its backward) needs whole rows in one tile: no K split there
-    const bool allow_split = (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) == 0;
-    if (pair) {
+    const int row = (d->epilogue & MG_EPI_SOFTMAX) ? mg::kRowSoftmax
+                    : (d->epilogue & mg::kEpiSoftmaxBwd) ? mg::kRowSoftmaxBwd : mg::kRowNone;
+    const bool allow_split = row == mg::kRowNone;
+    auto go = [&](auto bn_c, auto pair_c, auto row_c) {
+        return launch_tc<decltype(bn_c)::value, decltype(pair_c)::value, decltype(row_c)::value>(
+            dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+    };
+    using T = std::true_type;
+    using F = std::false_type;
+    auto by_width = [&](auto pair_c, auto row_c) -> mg_status {
         switch (bn) {
-        case 64: return launch_tc<64, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
-        case 128: return launch_tc<128, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
-        case 224: return launch_tc<224, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
-        default: return launch_tc<256, true>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+        case 64: return go(std::integral_constant<int, 64>{}, pair_c, row_c);
+        case 128: return go(std::integral_constant<int, 128>{}, pair_c, row_c);
+        case 256: return go(std::integral_constant<int, 256>{}, pair_c, row_c);
+        default: return fail(MG_ERR_UNSUPPORTED, "no kernel of tile width %d for this epilogue", bn);
         }
+    };
+    if (row == mg::kRowSoftmax) {
+        using R = std::integral_constant<int, mg::kRowSoftmax>;
+        return pair ? by_width(T{}, R{}) : by_width(F{}, R{});
     }
-    switch (bn) {
-    case 64: return launch_tc<64, false>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
-    case 128: return launch_tc<128, false>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
-    default: return launch_tc<256, false>(dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+    if (row == mg::kRowSoftmaxBwd) {
+        using R = std::integral_constant<int, mg::kRowSoftmaxBwd>;
+        return pair ? by_width(T{}, R{}) : by_width(F{}, R{});
     }
+    using R0 = std::integral_constant<int, mg::kRowNone>;
+    if (pair && bn == 224) return go(std::integral_constant<int, 224>{}, T{}, R0{});
+    return pair ? by_width(T{}, R0{}) : by_width(F{}, R0{});
 }
 
 mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias,
@@ -974,9 +1106,13 @@ mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* 
 // Shared by mg_matmul / mg_matmul_bias / mg_matmul_softmax: turns the
 // reference's rank-equalised contiguous shapes into a descriptor. Mirrors the
 // shape checks of Functional::matmul (tensor_ops.cpp:4559-4572, 4807-4818).
+// With `reduce`, out_shape may be 1 on a leading dim where the product is
+// not: that dim becomes a reduction dim (C batch stride 0), i.e. out receives
+// the product summed over it -- what `out += product` does in the reference
+// when out broadcasts to the product (tensor_ops.cpp:3393-3446).
 static mg_status seam_desc(mg_gemm_desc* d, const int32_t* out_shape, const int32_t* A_shape,
                            const int32_t* B_shape, const int32_t* bias_shape, int32_t rank,
-                           int32_t trans_a, int32_t trans_b)
+                           int32_t trans_a, int32_t trans_b, bool reduce = false)
 {
     if (!out_shape || !A_shape || !B_shape) return fail(MG_ERR_INVALID, "shape pointer is NULL");
     if (rank < 2) return fail(MG_ERR_INVALID, "rank %d < 2: shapes must be rank-equalised to >= 2", rank);
@@ -1005,7 +1141,9 @@ static mg_status seam_desc(mg_gemm_desc* d, const int32_t* out_shape, const int3
         if (!(A_shape[i] == B_shape[i] || A_shape[i] == 1 || B_shape[i] == 1))
             return fail(MG_ERR_INVALID, "leading dim %d not broadcastable (%d vs %d)", i, A_shape[i], B_shape[i]);
         const int32_t o = std::max(A_shape[i], B_shape[i]);
-        if (out_shape[i] != o) return fail(MG_ERR_INVALID, "out leading dim %d is %d, expected %d", i, out_shape[i], o);
+        if (out_shape[i] != o && !(reduce && out_shape[i] == 1))
+            return fail(MG_ERR_INVALID, "out leading dim %d is %d, expected %d%s", i, out_shape[i], o,
+                        reduce ? " or 1" : "");
         d->batch[j] = o;
         d->a_batch_stride[j] = A_shape[i] == 1 ? 0 : sa;
         d->b_batch_stride[j] = B_shape[i] == 1 ? 0 : sb;
@@ -1056,6 +1194,117 @@ mg_status mg_matmul_bias(float* out, const float* A, const float* B, const float
     return mg_gemm(&d, out, A, B, bias, stream);
 }
 
+mg_status mg_matmul_accumulate(float* out, const float* A, const float* B, const int32_t* out_shape,
+                               const int32_t* A_shape, const int32_t* B_shape, int32_t rank, int32_t trans_a,
+                               int32_t trans_b, float beta, void* stream)
+{
+    g_last_error.clear();
+    if (beta != 0.f && beta != 1.f) return fail(MG_ERR_INVALID, "beta must be 0 or 1 (got %g)", (double)beta);
+    mg_gemm_desc d;
+    mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, nullptr, rank, trans_a, trans_b, true);
+    if (s != MG_OK) return s;
+    d.beta = beta;
+    return mg_gemm(&d, out, A, B, nullptr, stream);
+}
+
+mg_status mg_sum_into(float* dst, const float* src, const int32_t* dst_shape, const int32_t* src_shape,
+                      int32_t rank, float beta, void* stream)
+{
+    g_last_error.clear();
+    if (!dst_shape || !src_shape) return fail(MG_ERR_INVALID, "shape pointer is NULL");
+    if (rank < 1 || rank > MG_MAX_BATCH_DIMS + 2)
+        return fail(MG_ERR_INVALID, "rank %d outside [1, %d]", rank, MG_MAX_BATCH_DIMS + 2);
+    if (beta != 0.f && beta != 1.f) return fail(MG_ERR_INVALID, "beta must be 0 or 1 (got %g)", (double)beta);
+    int64_t P = 1, R = 1, total = 1;
+    for (int i = 0; i < rank; ++i) {
+        if (dst_shape[i] < 0 || src_shape[i] < 0) return fail(MG_ERR_INVALID, "negative dimension at %d", i);
+        if (dst_shape[i] != src_shape[i] && dst_shape[i] != 1)
+            return fail(MG_ERR_INVALID, "dst dim %d is %d: it must be src's (%d) or 1", i, dst_shape[i],
+                        src_shape[i]);
+        P *= dst_shape[i];
+        total *= src_shape[i];
+    }
+    if (P == 0) return MG_OK;
+    if (!dst) return fail(MG_ERR_INVALID, "dst is NULL");
+    if (total > 0 && !src) return fail(MG_ERR_INVALID, "src is NULL");
+    R = total / P;
+    SumParams sp;
+    std::memset(&sp, 0, sizeof(sp));
+    // canonical dims of src (contiguous row-major): drop size-1 dims, merge
+    // neighbours of the same kind (kept: dst has the dim; reduced: dst has 1)
+    int kind[MG_MAX_BATCH_DIMS + 2];
+    int64_t size[MG_MAX_BATCH_DIMS + 2], stride[MG_MAX_BATCH_DIMS + 2];
+    int n = 0;
+    int64_t st = 1;
+    for (int i = rank - 1; i >= 0; --i) {
+        const int64_t sz = src_shape[i];
+        if (sz != 1) {
+            const int k = dst_shape[i] == 1 ? 1 : 0;
+            if (n > 0 && kind[n - 1] == k && stride[n - 1] * size[n - 1] == st) {
+                size[n - 1] *= sz;
+            } else {
+                kind[n] = k;
+                size[n] = sz;
+                stride[n] = st;
+                ++n;
+            }
+        }
+        st *= sz;
+    }
+    // outer first
+    for (int i = n - 1; i >= 0; --i) {
+        if (kind[i]) {
+            sp.rsize[sp.nr] = size[i];
+            sp.rstride[sp.nr++] = stride[i];
+        } else {
+            sp.ksize[sp.nk] = size[i];
+            sp.kstride[sp.nk++] = stride[i];
+        }
+    }
+    sp.src = src;
+    sp.dst = dst;
+    sp.P = P;
+    sp.R = R;
+    sp.beta = beta;
+    // [R][P]: one reduced dim outside one kept dim (or either alone)
+    sp.rows = (sp.nr <= 1 && sp.nk <= 1 && (n < 2 || kind[n - 1] == 1)) ? 1 : 0;
+    sp.vec = sp.rows && P % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0 &&
+             (reinterpret_cast<uintptr_t>(dst) & 15u) == 0;
+    DeviceState* dev = nullptr;
+    mg_status s = device_state(&dev);
+    if (s != MG_OK) return s;
+    cudaStream_t cs = (cudaStream_t)stream;
+    constexpr int kThreadsPerBlock = 256;
+    const int64_t lanes = sp.vec ? P / 4 : P;
+    const int64_t bx = (lanes + kThreadsPerBlock - 1) / kThreadsPerBlock;
+    if (bx >= (1ll << 31)) return fail(MG_ERR_UNSUPPORTED, "too many outputs (%lld)", (long long)P);
+    // enough blocks to keep every SM reading (4 per SM), each split >= 16 reduced rows
+    int64_t splits = std::max<int64_t>(1, (4ll * dev->sm_count + bx - 1) / bx);
+    splits = std::min<int64_t>(splits, std::max<int64_t>(1, R / 16));
+    splits = std::min<int64_t>(splits, 65535);
+    sp.rchunk = (R + splits - 1) / std::max<int64_t>(1, splits);
+    sp.splits = (int)(sp.rchunk > 0 ? (R + sp.rchunk - 1) / sp.rchunk : 1);
+    if (sp.splits < 1) sp.splits = 1;
+    Workspace ws;
+    ws.stream = stream;
+    ws.pool = dev->pool;
+    if (sp.splits > 1) {
+        sp.part = static_cast<float*>(ws.get((size_t)sp.splits * (size_t)P * sizeof(float)));
+        if (!sp.part) return fail(MG_ERR_ALLOC, "workspace allocation of %lld bytes failed",
+                                  (long long)sp.splits * P * 4);
+    }
+    sum_into_kernel<<<dim3((unsigned)bx, (unsigned)sp.splits), kThreadsPerBlock, 0, cs>>>(sp);
+    MG_CUDA_TRY(cudaGetLastError());
+    g_launches++;
+    if (sp.splits > 1) {
+        sum_parts_kernel<<<(unsigned)((P + kThreadsPerBlock - 1) / kThreadsPerBlock), kThreadsPerBlock, 0, cs>>>(
+            sp.part, dst, P, sp.splits, beta);
+        MG_CUDA_TRY(cudaGetLastError());
+        g_launches++;
+    }
+    return MG_OK;
+}
+
 mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const float* bias,
                             const int32_t* out_shape, const int32_t* A_shape, const int32_t* B_shape,
                             const int32_t* bias_shape, int32_t rank, int32_t trans_a, int32_t trans_b,
@@ -1086,11 +1335,14 @@ mg_status mg_matmul_softmax_backward(float* dS, const float* A, const float* B, 
     return gemm_impl(&d, dS, A, B, nullptr, stream, nullptr, 0, nullptr, P);
 }
 
-// mg_matmul without any allocation: the only scratch it may need (the padded
-// copy of an operand whose rows break TMA's 16-byte rule) comes from
-// g_noalloc_scratch. Its device address is looked up on this entry point's
-// first call on each device (cudaGetSymbolAddress, with that device current)
-// and cached; that first call should therefore come before any stream capture.
+// mg_matmul without any allocation: its scratch (the padded copy of an
+// operand whose rows break TMA's 16-byte rule, then the K-split partial slots
+// and counters) comes from g_noalloc_scratch; a re-layout that does not fit is
+// refused, split slots that do not fit leave the launch unsplit, and the lo
+// planes of MG_GEMM_PRESPLIT are never made. The array's device address is
+// looked up on this entry point's first call on each device
+// (cudaGetSymbolAddress, with that device current) and cached; that first
+// call should therefore come before any stream capture.
 mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const int32_t* out_shape,
                             const int32_t* A_shape, const int32_t* B_shape, int32_t rank,
                             int32_t trans_a, int32_t trans_b, void* stream)

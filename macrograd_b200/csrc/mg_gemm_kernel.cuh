@@ -121,8 +121,15 @@ struct GemmParams {
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
     int a_rank, b_rank;         // tensor-map ranks (2 + mapped batch dims)
     uint32_t idesc;
-    int nbd;                    // output batch dims
-    int bsize[kMaxBatchDims];
+    int nbd;                    // batch dims of the product
+    int bsize[kMaxBatchDims];   // their sizes over the output tiles (1 for a reduction dim)
+    // Reduction dims: batch dims of the product that C does not have (stride 0
+    // in C): C receives the sum over them, folded into the K loop -- K-block kb
+    // is K-block kb % kb_per of reduction step kb / kb_per, whose indices run
+    // row-major over rsize (1 for the other dims).
+    int rsize[kMaxBatchDims];
+    int red_steps;              // product of rsize (1: no reduction)
+    int kb_per;                 // K-blocks of one reduction step: ceil(K / 32)
     int8_t a_map[kMaxBatchDims], b_map[kMaxBatchDims];   // batch dim -> map dim (-1: broadcast)
     int32_t a_mult[kMaxBatchDims], b_mult[kMaxBatchDims];
     float* C;
@@ -193,6 +200,36 @@ __device__ __forceinline__ TileCoord decode_tile(int t, const GemmParams& p)
     return tc;
 }
 
+// Tensor-map coordinates (map dims 2, 3, 4) that batch multi-index idx adds
+// to operand X's loads.
+__device__ __forceinline__ void batch_coords(const GemmParams& p, const int* idx, const int8_t* map,
+                                             const int32_t* mult, int32_t* c)
+{
+#pragma unroll
+    for (int d = 0; d < kMaxBatchDims; ++d) {
+        if (d < p.nbd) {
+            const int32_t v = idx[d] * mult[d];
+            c[0] += map[d] == 0 ? v : 0;
+            c[1] += map[d] == 1 ? v : 0;
+            c[2] += map[d] == 2 ? v : 0;
+        }
+    }
+}
+
+// Multi-index of reduction step r (row-major over rsize; 0 on the other dims).
+__device__ __forceinline__ void reduction_index(int r, const GemmParams& p, int* idx)
+{
+#pragma unroll
+    for (int d = kMaxBatchDims - 1; d >= 0; --d) {
+        if (d < p.nbd && p.rsize[d] > 1) {
+            idx[d] = r % p.rsize[d];
+            r /= p.rsize[d];
+        } else {
+            idx[d] = 0;
+        }
+    }
+}
+
 // Output batch multi-index of a flat batch number (row-major over bsize).
 __device__ __forceinline__ void batch_index(int b, const GemmParams& p, int* idx)
 {
@@ -218,13 +255,11 @@ struct SharedState {
     uint64_t part_free;               // MMA issuer's CTA: every epilogue took the partial
     uint64_t part_full1;              // the same for the second accumulator (p.dbuf)
     uint64_t part_free1;
-    uint64_t row_max;                 // local (softmax): every epilogue thread posted its half-row max
-    uint64_t row_sum;                 // local (softmax): ... its half-row sum
-    uint64_t row_read;                // local (softmax): ... read its partner's sum
     uint64_t drain;
     uint32_t tmem_base;
     volatile int abort_flag;
     unsigned int tiles_stored;        // epilogue warps x tiles written to C (export mode)
+    uint64_t pair_bar[kEpiWarps / 2]; // row epilogues: epilogue warps w and w ^ 4 met (64 arrivals)
 };
 
 static_assert(sizeof(SharedState) <= kSharedStateBytes, "SharedState outgrew its slot");
@@ -317,14 +352,16 @@ __host__ __device__ constexpr int batch_of(int n, int b = 16)
 }
 
 // Warp-collective store of a 32 x 32 output block. The TMEM layout gives each
-// lane one row (v[j] = column gn0 + j of row gm); written as is, one warp
-// store touches 32 rows at 16 bytes each, which is expensive over NVLink. The
-// block is therefore staged in shared memory (16-byte chunks XOR-swizzled by
-// row: conflict-free both ways) and written back row-contiguous: each warp
-// store covers 4 rows x 128 bytes. Destinations: C, or with a fused
-// all-gather every rank's full C. All 32 lanes must call it.
+// lane one row (v[j] = column gn0 + j of row block_row0 + lane); written as
+// is, one warp store touches 32 rows at 16 bytes each, which is expensive over
+// NVLink. The block is therefore staged in shared memory (16-byte chunks
+// XOR-swizzled by row: conflict-free both ways) and written back
+// row-contiguous: each warp store covers 4 rows x 128 bytes. Destinations: C
+// (`blk` = the block's first row there, `rows` of its 32 rows inside the
+// matrix), or with a fused all-gather every rank's full C. All 32 lanes must
+// call it.
 __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerMaps& pm, float* stage,
-                                                const float* v, bool rok, float* crow, int64_t coff, int gm,
+                                                const float* v, float* blk, int rows, int64_t coff, int block_row0,
                                                 int gn0, int nvalid)
 {
     const int lane = threadIdx.x & 31;
@@ -333,7 +370,6 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
         reinterpret_cast<float4*>(stage + lane * 32)[q ^ (lane & 7)] =
             make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     __syncwarp();
-    const int block_row0 = gm - lane;   // first row of this warp's 32-row block
     const bool to_peers = p.npeers > 0 && !p.export_peers;   // the epilogue itself writes every rank's C
     if (to_peers && p.peer_tma && block_row0 + 32 <= p.M) {
         // The staging block is laid out as a TMA 128B-swizzled {32, 32} box:
@@ -352,20 +388,17 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
         return;
     }
     const int ndst = to_peers ? p.npeers : 1;
-    const int64_t peer_off = coff + (p.peer_row0 + gm) * p.ldc;
+    const int q = lane & 7;
+    const int r_lane = lane >> 3;   // row of this lane within each 4-row store
 #pragma unroll 1
     for (int dsti = 0; dsti < ndst; ++dsti) {
-        // this lane's row start in the destination
-        float* mine = to_peers ? p.peers[dsti] + peer_off : crow;
-        const int q = lane & 7;
+        float* base = to_peers ? p.peers[dsti] + coff + (p.peer_row0 + block_row0) * p.ldc : blk;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int r = i * 4 + (lane >> 3);
+            const int r = i * 4 + r_lane;
             const float4 val = reinterpret_cast<const float4*>(stage + r * 32)[q ^ (r & 7)];
-            float* row = reinterpret_cast<float*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(mine), r));
-            const bool ok = __shfl_sync(0xffffffffu, rok ? 1 : 0, r) != 0;
-            if (!ok || 4 * q >= nvalid) continue;
-            float* dst = row + gn0 + 4 * q;
+            if (r >= rows || 4 * q >= nvalid) continue;
+            float* dst = base + (int64_t)r * p.ldc + gn0 + 4 * q;
             if (4 * q + 4 <= nvalid && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
                 *reinterpret_cast<float4*>(dst) = val;
             } else {
@@ -521,64 +554,302 @@ __device__ __noinline__ void add_partials(const float* slot0, int nsib, size_t s
     }
 }
 
+// Meeting of the two epilogue warps that hold the two column halves of the
+// same 32 rows (warps w and w ^ 4; both read the same TMEM lanes): each has
+// posted what the other needs in its own staging block before calling. Only
+// the pair waits -- the other row groups run on -- and it waits suspended on
+// its mbarrier: the two warps share an SM sub-partition, so a polling loop
+// would take issue slots from the very warp it waits for. `meets` counts this
+// warp's meetings (both warps of a pair make the same number, so its parity
+// is the barrier's phase). Warp-collective.
+__device__ __forceinline__ bool pair_meet(SharedState* ss, int warp, unsigned int& meets, const GemmParams& p)
+{
+    const uint32_t bar = smem_u32(&ss->pair_bar[warp & 3]);
+    mbar_arrive(bar);   // release: this thread's posts
+    const bool met = wait_phase<1>(bar, meets & 1u, ss, p, kWaitEpilogueRows);
+    ++meets;
+    return __all_sync(0xffffffffu, met);
+}
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22; results below 2^-126 flush to 0). With e^t = 2^(t log2 e) it is
+// the row softmax's exponential: one FMA for the argument, one ex2.
+__device__ __forceinline__ float exp2_approx(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 // Row softmax passes over one thread's TMEM row, columns [c0, c1) in blocks
-// of 32. Column n's logit is alpha * acc[n] + brow[n * bcs] (brow null: no
-// bias); columns n >= lim (past N, or past the causal diagonal) are -inf and
-// their bias is never read. Out of line like the partial helpers: inlined,
-// their 32-value blocks and bias loads crowded the main epilogue loop's
-// registers in every kernel variant.
-__device__ __noinline__ float softmax_row_max(uint32_t t_row, int c0, int c1, int lim, float alpha,
-                                              const float* brow, int64_t bcs)
+// of 32 (c1 warp-uniform: the TMEM loads are warp-collective). Column n's
+// logit is alpha * acc[n] + brow[n * bcs] (brow null: no bias); columns
+// n >= lim (past N, or past the causal diagonal; per lane) are -inf and their
+// bias is never read. Two 32-column loads share one wait where two blocks
+// remain.
+__device__ __forceinline__ float logit_of(uint32_t acc, int n, int lim, float alpha, const float* brow, int64_t bcs)
+{
+    if (n >= lim) return -INFINITY;
+    float x = alpha * __uint_as_float(acc);
+    if (brow) x += brow[(int64_t)n * bcs];
+    return x;
+}
+
+// Max of the live logits. Without a bias it is taken on the raw
+// accumulators: rounding is monotone, so max_n fl(alpha acc[n]) =
+// fl(|alpha| max_n (sign(alpha) acc[n])) exactly. `biased` must be
+// warp-uniform (some lanes of a biased warp may have no bias row): the TMEM
+// loads inside its two branches are warp-collective.
+__device__ __forceinline__ float softmax_row_max(uint32_t t_row, int c0, int c1, int lim, float alpha,
+                                                 const float* brow, int64_t bcs, bool biased)
 {
     float mx = -INFINITY;
-    for (int c = c0; c < c1 && c < lim; c += 32) {
+    int c = c0;
+    if (!biased) {
+        const uint32_t sign = alpha < 0.f ? 0x80000000u : 0u;
+        for (; c + 32 < c1; c += 64) {
+            uint32_t r[32], q[32];
+            tmem_ld32x2(t_row + c, r, t_row + c + 32, q);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, c + j < lim ? __uint_as_float(r[j] ^ sign) : -INFINITY);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, c + 32 + j < lim ? __uint_as_float(q[j] ^ sign) : -INFINITY);
+        }
+        if (c < c1) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, c + j < lim ? __uint_as_float(r[j] ^ sign) : -INFINITY);
+        }
+        return mx == -INFINITY ? mx : fabsf(alpha) * mx;
+    }
+    for (; c + 32 < c1; c += 64) {
+        uint32_t r[32], q[32];
+        tmem_ld32x2(t_row + c, r, t_row + c + 32, q);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, logit_of(r[j], c + j, lim, alpha, brow, bcs));
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, logit_of(q[j], c + 32 + j, lim, alpha, brow, bcs));
+    }
+    if (c < c1) {
         uint32_t r[32];
         tmem_ld32(t_row + c, r);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const int n = c + j;
-            if (n < lim) {
-                float x = alpha * __uint_as_float(r[j]);
-                if (brow) x += brow[(int64_t)n * bcs];
-                mx = fmaxf(mx, x);
-            }
-        }
+        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, logit_of(r[j], c + j, lim, alpha, brow, bcs));
     }
     return mx;
 }
 
-// exp(logit - mx) back into the row's columns [c0, min(c1, ncols)) (0 for
-// the -inf columns); returns their sum, accumulated in column order.
-__device__ __noinline__ float softmax_row_exp(uint32_t t_row, int c0, int c1, int ncols, int lim, float alpha,
-                                              const float* brow, int64_t bcs, float mx)
+// exp(logit - mx) of one 32-column block, in place (0 for the -inf columns);
+// returns `sum` plus the block's values, added in column order.
+__device__ __forceinline__ float exp_block(uint32_t (&r)[32], int c, int lim, float alpha, const float* brow,
+                                           int64_t bcs, bool biased, float mx2, float sum)
 {
-    float sum = 0.f;
-    for (int c = c0; c < c1 && c < ncols; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c, r);
+    if (!biased) {
+        const float a2 = alpha * kLog2e;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-            const int n = c + j;
-            float e = 0.f;
-            if (n < lim) {
-                float x = alpha * __uint_as_float(r[j]);
-                if (brow) x += brow[(int64_t)n * bcs];
-                if (x != -INFINITY) e = expf(x - mx);
-            }
+            const float e = c + j < lim ? exp2_approx(fmaf(__uint_as_float(r[j]), a2, -mx2)) : 0.f;
             sum += e;
             r[j] = __float_as_uint(e);
         }
+        return sum;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float x = logit_of(r[j], c + j, lim, alpha, brow, bcs);
+        const float e = x != -INFINITY ? exp2_approx(fmaf(x, kLog2e, -mx2)) : 0.f;
+        sum += e;
+        r[j] = __float_as_uint(e);
+    }
+    return sum;
+}
+
+// exp(logit - mx) back into the row's columns [c0, c1); returns their sum,
+// accumulated in column order.
+__device__ __forceinline__ float softmax_row_exp(uint32_t t_row, int c0, int c1, int lim, float alpha,
+                                                 const float* brow, int64_t bcs, bool biased, float mx)
+{
+    const float mx2 = mx * kLog2e;
+    float sum = 0.f;
+    for (int c = c0; c < c1; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+        sum = exp_block(r, c, lim, alpha, brow, bcs, biased, mx2, sum);
         tmem_st32_async(t_row + c, r);
     }
     tmem_wait_st();   // the exps are in TMEM before the scaling pass reads them
     return sum;
 }
 
+// This lane's row of a 32 x 32 block of P (rows blk_row0 .., columns c ..):
+// the warp reads the block row-contiguously (each load instruction 4 rows x
+// 128 bytes) into its staging block, then each lane takes its own row -- the
+// transposition of the output stores, reversed. Rows at or past `rows` and
+// columns at or past `ncols` read as 0. Warp-collective; `stage` is free.
+__device__ __forceinline__ void load_row_block(const float* blk, int64_t ld, int rows, int ncols, bool vec,
+                                               float* stage, float (&pr)[32])
+{
+    const int lane = threadIdx.x & 31;
+    const int q = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = i * 4 + (lane >> 3);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rows) {
+            const float* src = blk + (int64_t)r * ld + 4 * q;
+            if (vec && 4 * q + 4 <= ncols) {
+                v = __ldg(reinterpret_cast<const float4*>(src));
+            } else {
+                if (4 * q + 0 < ncols) v.x = __ldg(src + 0);
+                if (4 * q + 1 < ncols) v.y = __ldg(src + 1);
+                if (4 * q + 2 < ncols) v.z = __ldg(src + 2);
+                if (4 * q + 3 < ncols) v.w = __ldg(src + 3);
+            }
+        }
+        reinterpret_cast<float4*>(stage + r * 32)[q ^ (r & 7)] = v;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float4 v = reinterpret_cast<const float4*>(stage + lane * 32)[k ^ (lane & 7)];
+        pr[4 * k] = v.x, pr[4 * k + 1] = v.y, pr[4 * k + 2] = v.z, pr[4 * k + 3] = v.w;
+    }
+    __syncwarp();   // every lane has its row before the block is reused
+}
+
+// Softmax backward, first pass: sum over this thread's row half of
+// P[n] * G[n], G = alpha * acc, in column order (columns [c0, c1), c1 <= N).
+__device__ __forceinline__ float softmax_bwd_rowsum(uint32_t t_row, int c0, int c1, const float* pblk, int64_t ld,
+                                                 int rows, int ncols, bool vec, float* stage, float alpha)
+{
+    float sum = 0.f;
+    for (int c = c0; c < c1; c += 32) {
+        float pr[32];
+        load_row_block(pblk + c, ld, rows, ncols - c, vec, stage, pr);
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (c + j < ncols) sum += pr[j] * (alpha * __uint_as_float(r[j]));
+    }
+    return sum;
+}
+
+// Softmax backward, second pass: dS = P * (G - sum) for this thread's row
+// half, columns [c0, c1), stored like any output block.
+__device__ __forceinline__ void softmax_bwd_out(const GemmParams& p, const PeerMaps& pm, uint32_t t_row, int c0, int c1,
+                                             const float* pblk, int rows, bool vec, float* stage, float sum,
+                                             float* cblk, int64_t coff, int wrow0)
+{
+    for (int c = c0; c < c1; c += 32) {
+        float pr[32];
+        load_row_block(pblk + c, p.ldc, rows, p.N - c, vec, stage, pr);
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pr[j] = pr[j] * (p.alpha * __uint_as_float(r[j]) - sum);
+        store_block_out(p, pm, stage, pr, cblk, rows, coff, wrow0, c, min(32, p.N - c));
+    }
+}
+
+// The row softmax epilogue of one tile, for the thread's row gm and its
+// column half [col0, col1) (TMEM row t_row; the warp's rows start at wrow0).
+// A row lives in one TMEM lane; warp w and its partner w ^ 4 hold its two
+// column halves. Each thread takes its half's max, the pair meets (pair_meet:
+// posts in the warps' staging blocks), exp(x - max) goes back into the row's
+// TMEM columns while summing, the pair meets for the sum (and once more before
+// the staging block is reused), then the scaled values leave. Semantics of
+// Tensor::softmax (tensor_ops.cpp:2093-2112): max, expf, sum in column order
+// (first half, then second), divide (here: multiply by the rounded
+// reciprocal). Returns false when a meeting gave up (abort). Out of line: one
+// call per tile keeps the main epilogue loop's registers free.
+__device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps& pm, SharedState* ss, int warp,
+                                          unsigned int& meet_seq, uint32_t t_row, int col0, int col1, int wrow0,
+                                          int gm, const float* bias_row, float* cblk, int brows, int64_t coff,
+                                          float* stage_w)
+{
+    const int lane = threadIdx.x & 31;
+    const int half = warp >> 2;
+    const bool causal = (p.epi & kEpiCausal) != 0;
+    float* xch = stage_w;                                                    // my posts
+    const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;   // partner's
+    // live columns: [0, N), and up to the diagonal when causal; wlim bounds
+    // every lane of the warp (rows wrow0 .. + 31), so the chunk loops -- and
+    // their warp-collective TMEM loads -- stay warp-uniform
+    const int lim = causal ? min(p.N, gm + 1) : p.N;
+    const int wlim = causal ? min(p.N, wrow0 + 32) : p.N;
+    const int c1 = min(col1, wlim);
+    // the bias path for the whole warp when any of its rows has a bias row
+    // (rows past M have none): a warp-uniform choice of code with collective loads
+    const bool biased = __any_sync(0xffffffffu, bias_row != nullptr);
+    float mx = softmax_row_max(t_row, col0, c1, lim, p.alpha, bias_row, p.bias_cs, biased);
+    xch[lane] = mx;
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    mx = fmaxf(mx, pxch[lane]);
+    float sum = softmax_row_exp(t_row, col0, c1, lim, p.alpha, bias_row, p.bias_cs, biased, mx);
+    xch[32 + lane] = sum;
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    // the row's sum: first half's columns, then the second half's
+    sum = half ? pxch[32 + lane] + sum : sum + pxch[32 + lane];
+    // the partner has read this block before the stores reuse it
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    const float inv = 1.f / sum;
+    const float dead = 0.f * inv;   // columns no lane of the warp reaches (NaN if the whole row is)
+    for (int c = col0; c < col1 && c < p.N; c += 32) {
+        float v[32];
+        if (c < wlim) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = dead;
+        }
+        store_block_out(p, pm, stage_w, v, cblk, brows, coff, wrow0, c, min(32, p.N - c));
+    }
+    return true;
+}
+
+// The fused softmax backward of one tile (dP = dO V^T, N <= BN, one n-tile):
+// dS = P * (dP - rowsum(P * dP)), the derivative SoftOp::_backward applies
+// (tensor_ops.cpp:2056-2059), P read from p.aux (laid out like C) as
+// row-contiguous 32 x 32 blocks through the warp's staging block
+// (load_row_block). The two column halves of a row meet like the forward
+// softmax's. Arguments as softmax_tile.
+__device__ __forceinline__ bool softmax_bwd_tile(const GemmParams& p, const PeerMaps& pm, SharedState* ss, int warp,
+                                              unsigned int& meet_seq, uint32_t t_row, int col0, int col1, int wrow0,
+                                              float* cblk, int64_t coff, float* stage_w)
+{
+    const int lane = threadIdx.x & 31;
+    const int half = warp >> 2;
+    float* xch = stage_w;
+    const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;
+    const int wrows = max(0, min(32, p.M - wrow0));     // the warp's rows inside the matrix
+    const float* pblk = p.aux + coff + (int64_t)min(wrow0, max(p.M - 1, 0)) * p.ldc;
+    const bool pvec = (p.ldc & 3) == 0 && (coff & 3) == 0 && (reinterpret_cast<uintptr_t>(p.aux) & 15u) == 0;
+    const int c1 = min(col1, p.N);
+    float sum = softmax_bwd_rowsum(t_row, col0, c1, pblk, p.ldc, wrows, p.N, pvec, stage_w, p.alpha);
+    xch[lane] = sum;
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    sum = half ? pxch[lane] + sum : sum + pxch[lane];   // first half's columns first
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    softmax_bwd_out(p, pm, t_row, col0, c1, pblk, wrows, pvec, stage_w, sum, cblk, coff, wrow0);
+    return true;
+}
+
 // tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
 // tmBlo map their lo planes (same layout), which the producer loads next to
 // the raw tiles instead of the split warps computing them.
 
-template <int BN, bool kPair>
+// kRow: the row epilogue this instantiation carries -- kRowNone (alpha, bias,
+// beta), kRowSoftmax (softmax_tile) or kRowSoftmaxBwd (softmax_bwd_tile) --
+// so that each variant holds only its own epilogue code.
+enum : int { kRowNone = 0, kRowSoftmax = 1, kRowSoftmaxBwd = 2 };
+
+template <int BN, bool kPair, int kRow>
 __global__ void __launch_bounds__(kThreads, 1)
     mg_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
@@ -621,12 +892,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(smem_u32(&ss->part_free), kEpiThreads * (kPair ? 2 : 1));
         mbar_init(smem_u32(&ss->part_full1), 1);
         mbar_init(smem_u32(&ss->part_free1), kEpiThreads * (kPair ? 2 : 1));
-        mbar_init(smem_u32(&ss->row_max), kEpiThreads);
-        mbar_init(smem_u32(&ss->row_sum), kEpiThreads);
-        mbar_init(smem_u32(&ss->row_read), kEpiThreads);
         mbar_init(smem_u32(&ss->drain), 1);
         ss->abort_flag = 0;
         ss->tiles_stored = 0u;
+        for (int q = 0; q < kEpiWarps / 2; ++q) mbar_init(smem_u32(&ss->pair_bar[q]), 64);
         mbar_fence_init();
     }
     if (warp == kProducerWarp && lane == 0) {
@@ -668,22 +937,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const TileCoord tc = decode_tile(u.tile, p);
                 int idx[kMaxBatchDims];
                 batch_index(tc.batch, p, idx);
-                int32_t a2 = 0, a3 = 0, a4 = 0, b2 = 0, b3 = 0, b4 = 0;
-#pragma unroll
-                for (int d = 0; d < kMaxBatchDims; ++d) {
-                    if (d < p.nbd) {
-                        const int32_t va = idx[d] * p.a_mult[d];
-                        const int32_t vb = idx[d] * p.b_mult[d];
-                        a2 += p.a_map[d] == 0 ? va : 0;
-                        a3 += p.a_map[d] == 1 ? va : 0;
-                        a4 += p.a_map[d] == 2 ? va : 0;
-                        b2 += p.b_map[d] == 0 ? vb : 0;
-                        b3 += p.b_map[d] == 1 ? vb : 0;
-                        b4 += p.b_map[d] == 2 ? vb : 0;
-                    }
-                }
+                int32_t ta[3] = {0, 0, 0}, tb[3] = {0, 0, 0};   // the tile's batch coordinates
+                batch_coords(p, idx, p.a_map, p.a_mult, ta);
+                batch_coords(p, idx, p.b_map, p.b_mult, tb);
+                int32_t a2 = ta[0], a3 = ta[1], a4 = ta[2], b2 = tb[0], b3 = tb[1], b4 = tb[2];
                 const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
                 const int n0 = tc.nt * BN + (int)rank * L::kBRows;
+                int red_step = -1;
                 for (int kb = u.kb0; kb < u.kb1; ++kb) {
                     if (!wait_phase<0>(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
                         ok = false;
@@ -691,7 +951,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     const uint32_t fb = smem_u32(&ss->full[stage]);
                     mbar_arrive_expect_tx(fb, (L::kLoadA + L::load_b(p.b_mn != 0)) * (p.presplit ? 2u : 1u));
-                    const int k0 = kb * kBK;
+                    int kk = kb;
+                    if (p.red_steps > 1) {
+                        // K-block kk of reduction step r: the operands' batch
+                        // coordinates move to that step's matrices
+                        const int r = kb / p.kb_per;
+                        kk = kb - r * p.kb_per;
+                        if (r != red_step) {
+                            red_step = r;
+                            int ridx[kMaxBatchDims];
+                            reduction_index(r, p, ridx);
+                            int32_t ra[3] = {ta[0], ta[1], ta[2]}, rb[3] = {tb[0], tb[1], tb[2]};
+                            batch_coords(p, ridx, p.a_map, p.a_mult, ra);
+                            batch_coords(p, ridx, p.b_map, p.b_mult, rb);
+                            a2 = ra[0], a3 = ra[1], a4 = ra[2], b2 = rb[0], b3 = rb[1], b4 = rb[2];
+                        }
+                    }
+                    const int k0 = kk * kBK;
                     // raw tiles, and in pre-split mode the lo tiles one region higher
                     for (int plane = 0; plane < (p.presplit ? 2 : 1); ++plane) {
                         const CUtensorMap* ma = plane ? &tmAlo : &tmA;
@@ -936,10 +1212,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* stage_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes) +
                          warp * kStageFloatsPerWarp;                  // this warp's store staging block
         const bool has_bias = (p.epi & kEpiBias) != 0;
-        const bool softmax = (p.epi & kEpiSoftmax) != 0;
-        const bool softmax_bwd = (p.epi & kEpiSoftmaxBwd) != 0;
+        constexpr bool softmax = kRow == kRowSoftmax;
+        constexpr bool softmax_bwd = kRow == kRowSoftmaxBwd;
         uint32_t chunk_phase = 0;
-        uint32_t row_phase = 0;   // softmax: one phase of row_max / row_sum / row_read per tile
+        unsigned int meet_seq = 0;   // row epilogues: meetings with the partner warp so far
         bool ok = true;
         Unit u;
         for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
@@ -1031,6 +1307,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n0 = tc.nt * BN;
             const int gm = m0 + row;
             const bool rok = gm < p.M;
+            // this warp's 32-row output block: its first row in C (export
+            // mode: this GPU's full C, at this rank's row offset) and how many
+            // of its rows are inside the matrix
+            const int wrow0 = m0 + sub * 32;
+            const int brows = max(0, min(32, p.M - wrow0));
+            float* cblk = p.C + coff + (int64_t)(brows > 0 ? wrow0 + (p.export_peers ? p.peer_row0 : 0) : 0) * p.ldc;
             // export mode: this GPU's full C, at this rank's row offset
             const int64_t crow_idx = rok ? gm + (p.export_peers ? p.peer_row0 : 0) : 0;
             float* crow = p.C + coff + crow_idx * p.ldc;
@@ -1038,84 +1320,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the result, column 0: the master, or (p.dbuf) this tile's accumulator
             const uint32_t t_row = lane_base + (uint32_t)(p.dbuf ? rg * BN : BN);
 
-            if (softmax) {
-                // Row softmax (N <= BN, one n-tile). A row lives in one TMEM
-                // lane; warp w and its partner w ^ 4 hold its two column
-                // halves. Each thread reduces its half, the halves meet
-                // through the warps' staging blocks (bounded mbarrier waits),
-                // exp(x - max) goes back into the master once, then the scaled
-                // values leave. Semantics of Tensor::softmax: max, exp, sum,
-                // divide (here: multiply by the rounded reciprocal).
-                const bool causal = (p.epi & kEpiCausal) != 0;
-                float* xch = stage_w;                                                    // my posts
-                const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;   // partner's
-                // every epilogue thread of the CTA has arrived on `bar` this tile
-                auto rows_meet = [&](uint64_t* bar) {
-                    mbar_arrive(smem_u32(bar));
-                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueRows);
-                    return __all_sync(0xffffffffu, met);
-                };
-                // live columns: [0, N), and up to the diagonal when causal
-                const int lim = causal ? min(p.N, gm + 1) : p.N;
-                const float* bias_row = has_bias && rok ? brow : nullptr;
-                float mx = softmax_row_max(t_row, 32 * c_lo, 32 * c_hi, lim, p.alpha, bias_row, p.bias_cs);
-                xch[lane] = mx;
-                if (!rows_meet(&ss->row_max)) { ok = false; break; }
-                mx = fmaxf(mx, pxch[lane]);
-                float sum = softmax_row_exp(t_row, 32 * c_lo, 32 * c_hi, p.N, lim, p.alpha, bias_row, p.bias_cs, mx);
-                xch[32 + lane] = sum;
-                if (!rows_meet(&ss->row_sum)) { ok = false; break; }
-                // the row's sum: first half's columns, then the second half's
-                sum = half ? pxch[32 + lane] + sum : sum + pxch[32 + lane];
-                // the partner has read this block before the stores reuse it
-                if (!rows_meet(&ss->row_read)) { ok = false; break; }
-                row_phase ^= 1u;
-                const float inv = 1.f / sum;
-                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_row + c, r);
-                    float v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * inv;
-                    store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
+            if constexpr (softmax) {
+                // row softmax (N <= BN, one n-tile): softmax_tile
+                if (!softmax_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, wrow0, gm,
+                                  has_bias && rok ? brow : nullptr, cblk, brows, coff, stage_w)) {
+                    ok = false;
+                    break;
                 }
-            } else if (softmax_bwd) {
-                // Softmax backward fused into dP = dO V^T (N <= BN, one n-tile):
-                // dS = P * (dP - rowsum(P * dP)), the derivative SoftOp::_backward
-                // applies (tensor_ops.cpp:2056-2059), P read from p.aux (laid out
-                // like C). The two column halves of a row meet like the forward
-                // softmax's: each posts its partial row sum in its staging block.
-                float* xch = stage_w;
-                const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;
-                const float* prow = p.aux + coff + (int64_t)(rok ? gm : 0) * p.ldc;
-                auto rows_meet = [&](uint64_t* bar) {
-                    mbar_arrive(smem_u32(bar));
-                    const bool met = wait_phase<1>(smem_u32(bar), row_phase, ss, p, kWaitEpilogueRows);
-                    return __all_sync(0xffffffffu, met);
-                };
-                float sum = 0.f;
-                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_row + c, r);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (rok && c + j < p.N) sum += __ldg(prow + c + j) * (p.alpha * __uint_as_float(r[j]));
-                }
-                xch[lane] = sum;
-                if (!rows_meet(&ss->row_max)) { ok = false; break; }
-                sum = half ? pxch[lane] + sum : sum + pxch[lane];   // first half's columns first
-                if (!rows_meet(&ss->row_read)) { ok = false; break; }
-                row_phase ^= 1u;
-                for (int c = 32 * c_lo; c < 32 * c_hi && c < p.N; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(t_row + c, r);
-                    float v[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float pv = (rok && c + j < p.N) ? __ldg(prow + c + j) : 0.f;
-                        v[j] = pv * (p.alpha * __uint_as_float(r[j]) - sum);
-                    }
-                    store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, c, min(32, p.N - c));
+            } else if constexpr (softmax_bwd) {
+                // fused softmax backward (N <= BN, one n-tile): softmax_bwd_tile
+                if (!softmax_bwd_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, wrow0, cblk, coff,
+                                      stage_w)) {
+                    ok = false;
+                    break;
                 }
             } else {
                 for (int c = 32 * c_lo; c < 32 * c_hi; c += 32) {
@@ -1137,7 +1354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j)
                             if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
                     }
-                    store_block_out(p, pm, stage_w, v, rok, crow, coff, gm, gn0, nvalid);
+                    store_block_out(p, pm, stage_w, v, cblk, brows, coff, wrow0, gn0, nvalid);
                 }
             }
             tc_fence_before();

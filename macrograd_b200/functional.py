@@ -1,16 +1,17 @@
 """Host-side mirror of Macrograd's matmul API over the sm_100a library.
 
 Mirrors, for torch CUDA tensors (torch provides device memory and streams;
-every GEMM runs in libmg_gemm.so -- torch arithmetic appears only in
-matmul_backward's non-GEMM steps: the bias gradient sum(dC) and the `+=`
-reduction of a broadcast operand's gradient when its batch cannot fold into
-K, the reference's own separate passes there, tensor_ops.cpp:3345-3451):
+every GEMM and every gradient reduction runs in libmg_gemm.so -- no torch
+arithmetic on the path):
   matmul(mat0, mat1, transA, transB)            Functional::matmul
       macrograd/source/tensor_ops.cpp:4482-4694
   matmul(mat0, mat1, bias, transA, transB)      Functional::matmul with bias
       macrograd/source/tensor_ops.cpp:4700-4949
   matmul_backward(...)                          MatMulOp / MatMulBiasOp::_backward
-      macrograd/source/tensor_ops.cpp:4504-4517, 4723-4737
+      macrograd/source/tensor_ops.cpp:4504-4517, 4723-4737, each gradient
+      GEMM accumulating straight into its gradient (mg_matmul_accumulate),
+      the bias gradient summed by mg_sum_into (the `+=` of
+      tensor_ops.cpp:3345-3451)
   attention_scores(...)                         matmul(Q/sqrt(d), K, mask, false, true)
       followed by softmax(-1), mini_shakespeare/include/transformer.h:233-234
   matmul_view(...)                              the same product on strided views (the
@@ -24,6 +25,7 @@ itself always runs in libmg_gemm.so (mg_matmul / mg_matmul_bias / mg_gemm).
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Optional, Sequence, Tuple
 
 import torch
@@ -327,56 +329,53 @@ def matmul_view(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = 
 
 
 # ------------------------------------------------------------------ backward
-def _fold_batch(x_shape, y_shape, out_target, tX, tY):
-    """When a gradient's target is broadcast over every leading dim while the
-    GEMM operands are batched, sum_b X_b^T Y_b is one GEMM with the batch
-    folded into K -- provided the two operands stack their batch along the
-    contracted rows (stored K-rows contiguous). Returns the 2-D storage shapes
-    or None."""
-    if len(out_target) <= 2 or any(d != 1 for d in out_target[:-2]):
-        return None
-    nb = 1
-    for d in x_shape[:-2]:
-        nb *= d
-    # only stackable when the contracted dim is the stored ROW dim of both
-    # operands: X stored [.., K, M] with tX, Y stored [.., K, N] without tY
-    if not tX or tY:
-        return None
-    if list(x_shape[:-2]) != list(y_shape[:-2]):
-        return None
-    return [nb * x_shape[-2], x_shape[-1]], [nb * y_shape[-2], y_shape[-1]]
-
-
 def _grad_gemm(X: torch.Tensor, Y: torch.Tensor, tX: bool, tY: bool, target_shape,
                accumulate: Optional[torch.Tensor], stream) -> torch.Tensor:
-    """matmul(X, Y, tX, tY) reduced to target_shape (the `+=` of
-    tensor_ops.cpp:3345-3451), optionally accumulated into `accumulate`."""
-    folded = _fold_batch(list(X.shape), list(Y.shape), list(target_shape), tX, tY)
+    """`grad += matmul(X, Y, tX, tY)` of MatMulOp::_backward
+    (tensor_ops.cpp:4504-4517) as ONE library call (mg_matmul_accumulate):
+    the product is summed over the leading dims where target_shape (the
+    rank-equalised shape of the operand whose gradient this is) is 1 -- the
+    reference's `+=` broadcast reduction, tensor_ops.cpp:3345-3451 -- inside
+    the GEMM's K loop, and added to `accumulate` (beta = 1) when given, else
+    written to a new tensor."""
     lib = _lib.load()
-    if folded is not None:
-        _check_operand(X, "gradient operand")
-        _check_operand(Y, "gradient operand")
-        if accumulate is not None:
-            _check_operand(accumulate, "gradient accumulator")
-        dev = _one_device(X, Y, accumulate, stream=stream)
-        xs, ys = folded
-        oshape = [xs[-1], ys[-1]]
-        dst = accumulate if accumulate is not None else torch.empty(target_shape, device=dev, dtype=torch.float32)
-        d = _lib.GemmDesc()
-        lib.mg_gemm_desc_init(ctypes.byref(d), oshape[0], oshape[1], xs[0], 1, 0)
-        d.beta = 1.0 if accumulate is not None else 0.0
-        with torch.cuda.device(dev):
-            check(lib.mg_gemm(ctypes.byref(d), _ptr(dst), _ptr(X), _ptr(Y), None, _stream_handle(X, stream)))
-        return dst
-    res = matmul(X, Y, None, tX, tY, stream=stream)
-    if list(res.shape) != list(target_shape):
-        # broadcast operand: reduce the batched temporary over its unit dims
-        dims = [i for i, (r, t) in enumerate(zip(res.shape, target_shape)) if t == 1 and r != 1]
-        res = res.sum(dim=dims, keepdim=True)
+    _check_operand(X, "gradient operand")
+    _check_operand(Y, "gradient operand")
     if accumulate is not None:
-        accumulate.add_(res)
-        return accumulate
-    return res
+        _check_operand(accumulate, "gradient accumulator")
+    dev = _one_device(X, Y, accumulate, stream=stream)
+    xs, ys = list(X.shape), list(Y.shape)
+    dst = accumulate if accumulate is not None else torch.empty(list(target_shape), device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        check(lib.mg_matmul_accumulate(_ptr(dst), _ptr(X), _ptr(Y), i32_array(target_shape), i32_array(xs),
+                                       i32_array(ys), len(xs), int(tX), int(tY),
+                                       ctypes.c_float(1.0 if accumulate is not None else 0.0),
+                                       _stream_handle(X, stream)))
+    return dst
+
+
+def sum_into(src: torch.Tensor, dst_shape: Sequence[int], accumulate: Optional[torch.Tensor] = None,
+             stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """`dst += src` where dst broadcasts to src (the reference's `+=`,
+    tensor_ops.cpp:3345-3451, squeeze direction): src summed over the dims
+    where dst_shape (rank-equalised to src) is 1, added to `accumulate` when
+    given, else written to a new tensor. One library call (mg_sum_into)."""
+    lib = _lib.load()
+    _check_operand(src, "src")
+    if accumulate is not None:
+        _check_operand(accumulate, "accumulator")
+    dev = _one_device(src, accumulate, stream=stream)
+    ss = list(src.shape)
+    ds = [1] * (len(ss) - len(dst_shape)) + list(dst_shape)
+    if len(ds) != len(ss):
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"dst shape {list(dst_shape)} has more dims than src {ss}")
+    dst = accumulate if accumulate is not None else torch.empty(ds, device=dev, dtype=torch.float32)
+    if accumulate is not None and accumulate.numel() != math.prod(ds):
+        raise MacrogradError(_lib.MG_ERR_INVALID, f"accumulator has {accumulate.numel()} elements, dst shape {ds}")
+    with torch.cuda.device(dev):
+        check(lib.mg_sum_into(_ptr(dst), _ptr(src), i32_array(ds), i32_array(ss), len(ss),
+                              ctypes.c_float(1.0 if accumulate is not None else 0.0), _stream_handle(src, stream)))
+    return dst
 
 
 def matmul_backward(A: torch.Tensor, B: torch.Tensor, dC: torch.Tensor, transA: bool = False,
@@ -384,18 +383,22 @@ def matmul_backward(A: torch.Tensor, B: torch.Tensor, dC: torch.Tensor, transA: 
                     bias_shape: Optional[Sequence[int]] = None,
                     need_a: bool = True, need_b: bool = True,
                     grad_a: Optional[torch.Tensor] = None, grad_b: Optional[torch.Tensor] = None,
+                    grad_bias: Optional[torch.Tensor] = None,
                     stream: Optional[torch.cuda.Stream] = None
                     ) -> Tuple[Optional[torch.Tensor], Optional[torch.Tensor], Optional[torch.Tensor]]:
     """Gradients of C = op(A) op(B) (+ bias) for an upstream dC, exactly the GEMMs
     MatMulOp::_backward issues (tensor_ops.cpp:4504-4517):
         dA = transA ? matmul(B, dC, transB, true) : matmul(dC, B, false, !transB)
         dB = transB ? matmul(dC, A, true, transA) : matmul(A, dC, !transA, false)
-    with A and B rank-equalised as the forward left them, then reduced to their
-    shapes like `internal_gradient() += ...`. A gradient whose operand was
-    broadcast over the batch (a weight) is one GEMM with the batch folded into
-    K instead of a batched temporary plus a reduction. grad_a / grad_b, when
-    given, are accumulated into (beta = 1) instead of freshly allocated."""
-    for name, g in (("grad_a", grad_a), ("grad_b", grad_b)):
+    with A and B rank-equalised as the forward left them, each reduced to its
+    operand's shape like `internal_gradient() += ...` inside the same GEMM (a
+    gradient whose operand was broadcast over the batch -- a weight -- sums
+    the batch in the GEMM's K loop: no batched temporary, no separate
+    reduction), and dbias = dC summed to the bias shape (MatMulBiasOp,
+    tensor_ops.cpp:4736) by the library's reduction. grad_a / grad_b /
+    grad_bias, when given, are accumulated into (beta = 1, the `+=`) instead of
+    freshly allocated."""
+    for name, g in (("grad_a", grad_a), ("grad_b", grad_b), ("grad_bias", grad_bias)):
         if g is not None:
             _check_operand(g, name)   # reshaped below as a view: the accumulation lands in it
     a, b, oshape, _, _ = equalize(A.shape, B.shape, transA, transB)
@@ -417,7 +420,8 @@ def matmul_backward(A: torch.Tensor, B: torch.Tensor, dC: torch.Tensor, transA: 
         dB = dB.reshape(B.shape)
     if has_bias:
         bs = equalize_bias(bias_shape, oshape)
-        dims = [i for i, (o, x) in enumerate(zip(oshape, bs)) if x == 1 and o != 1]
-        dbias = dCv.sum(dim=dims, keepdim=True) if dims else dCv.clone()
+        if not dCv.is_contiguous():
+            dCv = dCv.contiguous()
+        dbias = sum_into(dCv, bs, grad_bias.reshape(bs) if grad_bias is not None else None, stream=stream)
         dbias = dbias.reshape(bias_shape)
     return dA, dB, dbias

@@ -122,10 +122,15 @@ def scatter_matmul(A_local: torch.Tensor, B: torch.Tensor, peers: PeerRows, row0
     d = _lib.GemmDesc()
     lib.mg_gemm_desc_init(ctypes.byref(d), M, N, K, 0, 0)
     d.ldc = full.stride(0)
+    if stream is not None and torch.device(stream.device) != A_local.device:
+        raise ValueError(f"scatter_matmul: the stream is on {stream.device}, the operands on {A_local.device}")
     s = stream if stream is not None else torch.cuda.current_stream(A_local.device)
-    _lib.check(lib.mg_gemm_scatter_rows(ctypes.byref(d), ctypes.c_void_p(A_local.data_ptr()),
-                                        ctypes.c_void_p(B.data_ptr()), None, peers.array, len(peers.ptrs),
-                                        int(row0), int(full.shape[0]), ctypes.c_void_p(s.cuda_stream)))
+    # the library resolves its per-device state (and the K split's resident
+    # CTAs) from the current device: make it the operands' one
+    with torch.cuda.device(A_local.device):
+        _lib.check(lib.mg_gemm_scatter_rows(ctypes.byref(d), ctypes.c_void_p(A_local.data_ptr()),
+                                            ctypes.c_void_p(B.data_ptr()), None, peers.array, len(peers.ptrs),
+                                            int(row0), int(full.shape[0]), ctypes.c_void_p(s.cuda_stream)))
 
 
 def sharded_matmul(A_local: torch.Tensor, B: torch.Tensor, full_out: Optional[torch.Tensor] = None,

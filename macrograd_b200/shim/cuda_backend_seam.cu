@@ -6,7 +6,9 @@
 // defines kernel_ops::matmul / matmul_bias from kernel_ops_matmul.inc in the
 // same translation unit (so the seam sees `stream`, MemPool and
 // MACROGRAD_CHECK exactly as the replaced code did). The renamed cuBLASLt
-// functions are dead code: nothing calls them.
+// functions are dead code: nothing calls them, and the cuBLASLt symbols they
+// name resolve to the never-called stand-ins of cublaslt_absent.c, so the
+// drop-in library does not link cuBLASLt.
 #define matmul mg_unused_cublaslt_matmul
 #define matmul_bias mg_unused_cublaslt_matmul_bias
 #include "cuda_backend.cu"

@@ -61,7 +61,7 @@ def seam_library():
     global _lib
     if _lib is None:
         if not os.path.exists(SEAM):
-            raise FileNotFoundError(f"{SEAM} is missing: build it with `make -C macrograd_b200/shim`")
+            raise FileNotFoundError(f"{SEAM} is missing: build it with `make -C macrograd_b200/shim REF=/path/to/macrograd`")
         from . import _lib as mglib
 
         mglib.load()

@@ -1,6 +1,7 @@
 """Generates tests/golden/matmul_golden.npz from the REFERENCE ITSELF.
 
-Run in a container that has the reference sources, after `make -C oracle ref`
+Run in a container that has the reference sources, after
+`make -C oracle ref REF=/path/to/macrograd`
 built oracle/_ref/libmgref.so from them:
 
     python tests/golden/make_golden.py

@@ -138,3 +138,24 @@ def test_softmax_backward_entry_errors_return_status():
     lib.mg_gemm_desc_init(ctypes.byref(d), 4, 300, 8, 0, 1)
     d.epilogue = 8
     assert lib.mg_gemm(ctypes.byref(d), buf, buf, buf, None, None) == _lib.MG_ERR_INVALID
+
+
+def _needed(path):
+    out = subprocess.run(["readelf", "-d", path], capture_output=True, text=True, check=True).stdout
+    return re.findall(r"\(NEEDED\)\s+Shared library: \[([^\]]+)\]", out)
+
+
+def test_no_cublas_in_the_product_libraries():
+    """No cuBLAS on the product path: neither the GEMM library nor the drop-in
+    build of the reference (whose renamed cuBLASLt bodies are never called and
+    resolve to shim/cublaslt_absent.c) needs a cuBLAS library at load time."""
+    mg.load(build_if_missing=True)
+    libs = [_lib.lib_path()]
+    seam = os.path.join(ROOT, "macrograd_b200", "shim", "_build", "libmacrograd_seam.so")
+    if os.path.exists(seam):
+        libs.append(seam)
+    for path in libs:
+        needed = _needed(path)
+        assert not [n for n in needed if "cublas" in n.lower()], f"{os.path.basename(path)} needs {needed}"
+    if len(libs) == 2:
+        assert any("mg_gemm" in n for n in _needed(seam)), "the drop-in build must link libmg_gemm.so"

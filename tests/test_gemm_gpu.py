@@ -444,12 +444,19 @@ def test_config2_linear_layer(mode):
     Y = host(F.matmul(Xg, Wg, cuda(b), False, True))
     rows = slice(8000, 8192)
     assert_close(Y[rows], ob.oracle_matmul(X[rows], W, False, True, b), mode, "cfg2 Y rows")
-    dX, dW, db = F.matmul_backward(Xg, Wg, dYg, False, True, True, (1536,))
+    # the weight and bias gradients accumulate into existing ones (beta = 1),
+    # as `internal_gradient() += ...` does in MatMulBiasOp::_backward
+    prevW = ob.seeded_normal((1536, 384), 4002)
+    prevb = ob.seeded_normal((1536,), 5002)
+    gW, gb = cuda(prevW), cuda(prevb)
+    dX, dW, db = F.matmul_backward(Xg, Wg, dYg, False, True, True, (1536,), grad_b=gW, grad_bias=gb)
+    assert dW.data_ptr() == gW.data_ptr() and db.data_ptr() == gb.data_ptr()
     assert_close(host(dX)[rows], ob.oracle_matmul(dY[rows], W), mode, "cfg2 dX rows")
     cols = slice(96, 160)
     rdW = ob.oracle_matmul(dY, np.ascontiguousarray(X[:, cols]), True, False)
-    assert_close(host(dW)[:, cols], rdW, mode, "cfg2 dW cols")
-    assert_close(host(db), ob.oracle_reduce_to(dY, [1, 1536]).reshape(1536), _lib.MG_MODE_TF32X3, "cfg2 db")
+    assert_close(host(dW)[:, cols], prevW[:, cols] + rdW, mode, "cfg2 dW cols (+=)")
+    assert_close(host(db), prevb + ob.oracle_reduce_to(dY, [1, 1536]).reshape(1536), _lib.MG_MODE_TF32X3,
+                 "cfg2 db (+=)")
 
 
 def test_config3_attention_forward_and_backward():

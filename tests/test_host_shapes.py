@@ -32,12 +32,33 @@ def test_bias_equalize():
         F.equalize_bias((3,), [4, 5])
 
 
-def test_fold_batch_for_broadcast_weight_gradient():
-    # dW of A[8,256,384] @ W[384,384]: matmul(A, dC, true, false) summed over the batch
-    assert F._fold_batch([8, 256, 384], [8, 256, 384], [1, 384, 384], True, False) == \
-        ([2048, 384], [2048, 384])
-    assert F._fold_batch([8, 256, 384], [8, 256, 384], [8, 384, 384], True, False) is None
-    assert F._fold_batch([8, 384, 256], [8, 256, 384], [1, 384, 384], False, False) is None
+def test_accumulate_and_sum_into_refuse_bad_shapes_before_any_device_call():
+    """mg_matmul_accumulate (the gradient GEMM with its `+=` reduction) and
+    mg_sum_into (the bias gradient's reduction) check their shapes like the
+    reference's `+=` (a dim equal to the product's, or 1) and return
+    MG_ERR_INVALID -- no abort, no device touched (this runs without a GPU)."""
+    import ctypes
+
+    from macrograd_b200 import _lib
+    from macrograd_b200._lib import i32_array
+
+    lib = _lib.load(build_if_missing=True)
+    null = ctypes.c_void_p(0)
+    acc = lib.mg_matmul_accumulate
+    # product [8, 384, 384] of A^T[8,384,256] . dC[8,256,384]: out may be [8,..] or [1,..], not [2,..]
+    assert acc(null, null, null, i32_array([2, 384, 384]), i32_array([8, 256, 384]), i32_array([8, 256, 384]),
+               3, 1, 0, ctypes.c_float(1.0), null) == _lib.MG_ERR_INVALID
+    assert b"or 1" in lib.mg_last_error()
+    assert acc(null, null, null, i32_array([1, 384, 384]), i32_array([8, 256, 384]), i32_array([8, 256, 384]),
+               3, 1, 0, ctypes.c_float(0.5), null) == _lib.MG_ERR_INVALID   # beta 0 or 1 only
+    assert acc(null, null, null, i32_array([1, 384, 300]), i32_array([8, 256, 384]), i32_array([8, 256, 384]),
+               3, 1, 0, ctypes.c_float(1.0), null) == _lib.MG_ERR_INVALID   # wrong N
+    s = lib.mg_sum_into
+    assert s(null, null, i32_array([1, 3]), i32_array([4, 5]), 2, ctypes.c_float(0.0), null) == _lib.MG_ERR_INVALID
+    assert s(null, null, i32_array([1, 5]), i32_array([4, 5]), 2, ctypes.c_float(2.0), null) == _lib.MG_ERR_INVALID
+    assert s(null, null, i32_array([1, 5]), i32_array([4, 5]), 0, ctypes.c_float(0.0), null) == _lib.MG_ERR_INVALID
+    assert s(null, null, i32_array([1, 5]), i32_array([4, 5]), 2, ctypes.c_float(0.0), null) == _lib.MG_ERR_INVALID
+    assert b"NULL" in lib.mg_last_error()
 
 
 def test_view_layout_reads_strides_of_head_split_views():

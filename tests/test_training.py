@@ -21,10 +21,14 @@ BATCH, T, SEED = 4, 16, 11
 
 def _seam_or_skip():
     if not os.path.exists(training.SEAM):
-        # the drop-in build's recipe knows where the reference sources are; it
-        # fails (and the test skips) where they are absent
-        subprocess.run(["make", "-s", "-C", os.path.join(ob.ROOT, "macrograd_b200", "shim")],
-                       capture_output=True)
+        # the drop-in build compiles the reference sources; where they are
+        # absent it is not built (and the test skips)
+        import __graft_entry__
+
+        ref = __graft_entry__.reference_dir()
+        if ref is not None:
+            subprocess.run(["make", "-s", "-C", os.path.join(ob.ROOT, "macrograd_b200", "shim"), f"REF={ref}"],
+                           capture_output=True)
     if not os.path.exists(training.SEAM):
         pytest.skip("drop-in build not available (needs the reference sources at build time)")
 

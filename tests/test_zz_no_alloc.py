@@ -2,14 +2,18 @@
 cannot let the library allocate device memory during a call (runtimes that
 plan and own all device memory up front, latency-critical loops that must not
 touch an allocator). It takes its scratch -- the padded copy of an operand whose
-rows are not a multiple of 16 bytes -- from a fixed device buffer inside the
-library instead of allocating it.
+rows are not a multiple of 16 bytes, and the partial tiles of a K-split last
+wave with their counters -- from a fixed device buffer inside the library
+instead of allocating it.
 
 Checked through the C ABI against mg_matmul on cases that need that scratch,
 on two calls in a row (the buffer keeps the previous call's contents), with a
 counting allocator registered to show that mg_matmul allocates and
-mg_matmul_noalloc does not, and with an oversized request that must be
-refused before anything runs.
+mg_matmul_noalloc does not; on a long-K product whose single tile is split
+along K with its partial slots in the buffer (against the oracle, and bit for
+bit against mg_matmul's own split); on one whose re-laid-out operands leave no
+room for the slots, which must run unsplit; and with an oversized request that
+must be refused before anything runs.
 """
 import ctypes
 
@@ -93,6 +97,69 @@ def test_noalloc_matches_mg_matmul_two_calls_in_a_row(sa, sb, ta, tb):
             assert ob.frob_rel_err(got, ref) <= 1e-5, f"call {call_no}"
     finally:
         lib.mg_set_allocator(None, None, None)
+
+
+def _split_slots_bytes(bn, slots):
+    """Scratch of a K split with `slots` partial ranges: two 128 x bn fp32
+    tiles per slot, then two counters per slot (mg_gemm.cu setup_split)."""
+    return slots * 2 * 128 * bn * 4 + slots * 2 * 4
+
+
+@pytest.mark.parametrize("K", [8192])
+def test_noalloc_k_split_from_the_buffer_matches_oracle(K, monkeypatch):
+    """A[K,65]^T B[K,65]: one 65 x 65 output tile (single-SM kernel, tile width
+    128) on a 148-SM GPU, so the launch splits that tile into 8 K-ranges whose
+    7 partial tiles go through the fixed buffer, after both operands' padded
+    copies (rows of 65 floats): 2 x 8192 x 68 x 4 B + the slots, well inside it."""
+    lib = mg.load()
+    relayout = 2 * (K * 68 * 4 + 16)
+    assert relayout + 512 + _split_slots_bytes(128, 7) < _lib_scratch_bytes()
+    results = []
+    for call_no in range(2):
+        A_h = ob.seeded_uniform((K, 65), 950 + 10 * call_no)
+        B_h = ob.seeded_uniform((K, 65), 951 + 10 * call_no)
+        A, B = torch.from_numpy(A_h).cuda(), torch.from_numpy(B_h).cuda()
+        st, got = call(lib.mg_matmul_noalloc, A, B, True, False)
+        assert st == _lib.MG_OK, lib.mg_last_error()
+        st, split = call(lib.mg_matmul, A, B, True, False)
+        assert st == _lib.MG_OK, lib.mg_last_error()
+        monkeypatch.setenv("MG_GEMM_SPLIT", "0")
+        st, unsplit = call(lib.mg_matmul, A, B, True, False)
+        monkeypatch.delenv("MG_GEMM_SPLIT")
+        assert st == _lib.MG_OK, lib.mg_last_error()
+        got, split, unsplit = (x.cpu().numpy() for x in (got, split, unsplit))
+        ref = ob.oracle_matmul(A_h, B_h, True, False)
+        assert ob.frob_rel_err(got, ref) <= 1e-5, f"call {call_no}"
+        # the same plan as mg_matmul's: the partial ranges added in the same order
+        assert np.array_equal(got, split), f"call {call_no}: not mg_matmul's split result"
+        # ... and a different summation from the one-range launch: the split ran
+        assert not np.array_equal(got, unsplit), f"call {call_no}: the launch did not split"
+        results.append(got)
+    assert not np.array_equal(results[0], results[1])
+
+
+def test_noalloc_runs_unsplit_when_the_slots_do_not_fit(monkeypatch):
+    """The same product with K = 29312: the two padded copies take all but
+    ~0.7 MiB of the buffer, less than the 7 partial slots need, so the launch
+    must run without its K split -- bit for bit mg_matmul with the split off."""
+    lib = mg.load()
+    K = 29312
+    relayout = 2 * (K * 68 * 4 + 16) + 256
+    cap = _lib_scratch_bytes()
+    assert relayout <= cap < relayout + _split_slots_bytes(128, 7)
+    A_h = ob.seeded_uniform((K, 65), 970)
+    B_h = ob.seeded_uniform((K, 65), 971)
+    A, B = torch.from_numpy(A_h).cuda(), torch.from_numpy(B_h).cuda()
+    for call_no in range(2):
+        st, got = call(lib.mg_matmul_noalloc, A, B, True, False)
+        assert st == _lib.MG_OK, lib.mg_last_error()
+        monkeypatch.setenv("MG_GEMM_SPLIT", "0")
+        st, unsplit = call(lib.mg_matmul, A, B, True, False)
+        monkeypatch.delenv("MG_GEMM_SPLIT")
+        assert st == _lib.MG_OK, lib.mg_last_error()
+        got, unsplit = got.cpu().numpy(), unsplit.cpu().numpy()
+        assert np.array_equal(got, unsplit), f"call {call_no}"
+        assert ob.frob_rel_err(got, ob.oracle_matmul(A_h, B_h, True, False)) <= 1e-5
 
 
 def test_noalloc_refuses_requests_beyond_its_buffer():
