@@ -390,13 +390,20 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
     const int ndst = to_peers ? p.npeers : 1;
     const int q = lane & 7;
     const int r_lane = lane >> 3;   // row of this lane within each 4-row store
+    // the block's row pieces out of shared memory first, then the global stores
+    float4 vals[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = i * 4 + r_lane;
+        vals[i] = reinterpret_cast<const float4*>(stage + r * 32)[q ^ (r & 7)];
+    }
 #pragma unroll 1
     for (int dsti = 0; dsti < ndst; ++dsti) {
         float* base = to_peers ? p.peers[dsti] + coff + (p.peer_row0 + block_row0) * p.ldc : blk;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = i * 4 + r_lane;
-            const float4 val = reinterpret_cast<const float4*>(stage + r * 32)[q ^ (r & 7)];
+            const float4 val = vals[i];
             if (r >= rows || 4 * q >= nvalid) continue;
             float* dst = base + (int64_t)r * p.ldc + gn0 + 4 * q;
             if (4 * q + 4 <= nvalid && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
@@ -693,22 +700,31 @@ __device__ __forceinline__ void load_row_block(const float* blk, int64_t ld, int
 {
     const int lane = threadIdx.x & 31;
     const int q = lane & 7;
+    // all eight loads first, then the stores: a shared store between two
+    // global loads would hold the second back (the compiler cannot move a
+    // load above a store through a pointer that may alias it), turning one
+    // memory round trip per block into eight
+    float4 v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int r = i * 4 + (lane >> 3);
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (r < rows) {
             const float* src = blk + (int64_t)r * ld + 4 * q;
             if (vec && 4 * q + 4 <= ncols) {
-                v = __ldg(reinterpret_cast<const float4*>(src));
+                v[i] = __ldg(reinterpret_cast<const float4*>(src));
             } else {
-                if (4 * q + 0 < ncols) v.x = __ldg(src + 0);
-                if (4 * q + 1 < ncols) v.y = __ldg(src + 1);
-                if (4 * q + 2 < ncols) v.z = __ldg(src + 2);
-                if (4 * q + 3 < ncols) v.w = __ldg(src + 3);
+                if (4 * q + 0 < ncols) v[i].x = __ldg(src + 0);
+                if (4 * q + 1 < ncols) v[i].y = __ldg(src + 1);
+                if (4 * q + 2 < ncols) v[i].z = __ldg(src + 2);
+                if (4 * q + 3 < ncols) v[i].w = __ldg(src + 3);
             }
         }
-        reinterpret_cast<float4*>(stage + r * 32)[q ^ (r & 7)] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = i * 4 + (lane >> 3);
+        reinterpret_cast<float4*>(stage + r * 32)[q ^ (r & 7)] = v[i];
     }
     __syncwarp();
 #pragma unroll
