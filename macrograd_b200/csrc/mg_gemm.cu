@@ -589,14 +589,18 @@ bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, 
 
 template <int BN, bool kPair, int kRow>
 mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& malo,
-                    const CUtensorMap& mblo, mg::GemmParams& gp, const mg::PeerMaps& pm, cudaStream_t st,
-                    Workspace* ws, bool allow_split)
+                    const CUtensorMap& mblo, const CUtensorMap& mp, mg::GemmParams& gp, const mg::PeerMaps& pm,
+                    cudaStream_t st, Workspace* ws, bool allow_split)
 {
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
-    // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
-    const size_t fixed = 1024 + mg::kSharedStateBytes + (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4 + 64;
     const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);   // raw (+ lo) tiles
+    // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
+    // (+ the softmax backward's P ring, when two operand stages still fit)
+    size_t fixed = 1024 + mg::kSharedStateBytes + (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4 + 64;
+    const size_t ring = (size_t)mg::kPRingSlots * mg::kPSlotBytes;
+    if (kRow != mg::kRowSoftmaxBwd || (size_t)dev->max_smem < fixed + ring + 2 * per_stage) gp.p_tma = 0;
+    if (gp.p_tma) fixed += ring;
     int stages = (int)((size_t)(dev->max_smem - (int)fixed) / per_stage);
     stages = std::min(stages, mg::kMaxStages);
     if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
@@ -640,7 +644,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             cfg.attrs = attr2;
             cfg.numAttrs = 2;
             cfg.gridDim = dim3((unsigned)(2 * resident), 1, 1);
-            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm) == cudaSuccess) {
+            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, gp, pm) == cudaSuccess) {
                 g_launches++;
                 return MG_OK;
             }
@@ -654,7 +658,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         }
         const int pairs = std::max(1, std::min(gp.total_tiles, resident));
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm));
+        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, gp, pm));
     } else {
         const bool split_k = setup_split<BN>(gp, dev->sm_count, ws, st, allow_split);
         gp.dbuf = (!split_k && gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
@@ -669,7 +673,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             attr[0].val.cooperative = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, gp, pm) == cudaSuccess) {
+            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, gp, pm) == cudaSuccess) {
                 g_launches++;
                 return MG_OK;
             }
@@ -680,7 +684,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
         }
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
-        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, gp, pm);
+        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, mp, gp, pm);
         MG_CUDA_TRY(cudaGetLastError());
     }
     g_launches++;
@@ -1011,6 +1015,26 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.ldc = d->ldc;
     gp.bias = has_bias ? bias : nullptr;
     gp.aux = aux;
+    // softmax backward: P (laid out like C) streamed by TMA into the epilogue's
+    // ring, where its layout allows a tensor map (16-byte row pitch and batch
+    // strides, aligned base); otherwise the epilogue reads it directly
+    CUtensorMap mp = ma;
+    if (aux && !scatter) {
+        Operand px{aux, d->M, d->N, d->ldc, {0}};
+        for (int i = 0; i < nbd; ++i) px.bs[i] = d->c_batch_stride[i];
+        BatchMap pbm;
+        if (build_batch_map(nbd, d->batch, px.bs, &pbm) && tma_compatible(px, pbm) &&
+            tuning_int("MG_GEMM_P_TMA", 1, 0, 1)) {
+            s = encode_map(&mp, px, pbm, 0, 128);
+            if (s != MG_OK) return s;
+            gp.p_tma = 1;
+            gp.p_rank = 2 + pbm.nmap;
+            for (int i = 0; i < mg::kMaxBatchDims; ++i) {
+                gp.p_map[i] = pbm.map[i];
+                gp.p_mult[i] = pbm.mult[i];
+            }
+        }
+    }
     gp.bias_rs = d->bias_rs;
     gp.bias_cs = d->bias_cs;
     gp.alpha = d->alpha;
@@ -1072,7 +1096,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const bool allow_split = row == mg::kRowNone;
     auto go = [&](auto bn_c, auto pair_c, auto row_c) {
         return launch_tc<decltype(bn_c)::value, decltype(pair_c)::value, decltype(row_c)::value>(
-            dev, ma, mb, malo, mblo, gp, pm, st, &ws, allow_split);
+            dev, ma, mb, malo, mblo, mp, gp, pm, st, &ws, allow_split);
     };
     using T = std::true_type;
     using F = std::false_type;

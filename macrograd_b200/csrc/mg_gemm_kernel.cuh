@@ -85,6 +85,13 @@ constexpr int kExportWarp0 = 14;
 constexpr int kExportThreads = 64;
 constexpr int kThreads = 16 * 32;
 constexpr int kMaxBatchDims = 6;
+// Softmax backward with P loaded by TMA (GemmParams::p_tma): a ring of two
+// slots in shared memory after the epilogue staging blocks, each one step of
+// both column halves -- two boxes of 128 rows x 32 columns (128-byte rows,
+// 128-byte swizzle: the staging blocks' layout).
+constexpr int kPRingSlots = 2;
+constexpr uint32_t kPBoxBytes = 128u * 128u;
+constexpr uint32_t kPSlotBytes = 2u * kPBoxBytes;
 constexpr int kMaxPeers = 8;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
@@ -137,6 +144,10 @@ struct GemmParams {
     int64_t c_bs[kMaxBatchDims];
     const float* bias;
     const float* aux;           // kEpiSoftmaxBwd: the softmax output P, laid out like C
+    int p_tma;                  // kEpiSoftmaxBwd: P streamed by TMA (map tmP) into the P ring
+    int p_rank;                 // tmP's rank (2 + mapped batch dims)
+    int8_t p_map[kMaxBatchDims];
+    int32_t p_mult[kMaxBatchDims];
     int64_t bias_rs, bias_cs;
     int64_t bias_bs[kMaxBatchDims];
     float alpha, beta;
@@ -260,6 +271,8 @@ struct SharedState {
     volatile int abort_flag;
     unsigned int tiles_stored;        // epilogue warps x tiles written to C (export mode)
     uint64_t pair_bar[kEpiWarps / 2]; // row epilogues: epilogue warps w and w ^ 4 met (64 arrivals)
+    uint64_t p_full[kPRingSlots];     // softmax backward: a step of P landed in the ring slot
+    uint64_t p_empty[kPRingSlots];    // ... every epilogue warp is done with the slot
 };
 
 static_assert(sizeof(SharedState) <= kSharedStateBytes, "SharedState outgrew its slot");
@@ -856,6 +869,71 @@ __device__ __forceinline__ bool softmax_bwd_tile(const GemmParams& p, const Peer
     return true;
 }
 
+// The softmax backward of one tile with P streamed into the ring by the P
+// producer (p.p_tma): the same arithmetic and order as softmax_bwd_tile, P
+// read from the ring slot's box of this warp's column half (row sub * 32 +
+// lane, the staging layout) instead of from global memory. Each pass consumes
+// `nsteps` slots -- every step, also one past N -- and releases each slot once
+// the warp has its rows; `slot` / `phase` follow the ring across tiles.
+__device__ __forceinline__ bool softmax_bwd_tile_ring(const GemmParams& p, const PeerMaps& pm, SharedState* ss,
+                                                   int warp, unsigned int& meet_seq, int& slot, uint32_t& phase,
+                                                   int nsteps, uint32_t t_row, int col0, int wrow0, int brows,
+                                                   float* cblk, int64_t coff, float* stage_w)
+{
+    const int lane = threadIdx.x & 31;
+    const int half = warp >> 2;
+    const int row = (warp & 3) * 32 + lane;
+    float* xch = stage_w;
+    const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;
+    const float* ring = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(ss) + kSharedStateBytes +
+                                                       (size_t)kEpiWarps * kStageFloatsPerWarp * 4);
+    // this lane's 32 P values of the slot's box for this half; then the slot goes back
+    auto take = [&](float (&pr)[32]) -> bool {
+        const bool landed = wait_phase<1>(smem_u32(&ss->p_full[slot]), phase, ss, p, kWaitEpiloguePartial);
+        if (!__all_sync(0xffffffffu, landed)) return false;
+        const float* box = ring + (size_t)slot * (kPSlotBytes / 4) + (size_t)half * (kPBoxBytes / 4);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float4 v = reinterpret_cast<const float4*>(box + row * 32)[k ^ (row & 7)];
+            pr[4 * k] = v.x, pr[4 * k + 1] = v.y, pr[4 * k + 2] = v.z, pr[4 * k + 3] = v.w;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&ss->p_empty[slot]));
+        if (++slot == kPRingSlots) { slot = 0; phase ^= 1u; }
+        return true;
+    };
+    float sum = 0.f;
+    for (int s = 0; s < nsteps; ++s) {
+        const int c = col0 + 32 * s;
+        float pr[32];
+        if (!take(pr)) return false;
+        if (c < p.N) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (c + j < p.N) sum += pr[j] * (p.alpha * __uint_as_float(r[j]));
+        }
+    }
+    xch[lane] = sum;
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    sum = half ? pxch[lane] + sum : sum + pxch[lane];   // first half's columns first
+    if (!pair_meet(ss, warp, meet_seq, p)) return false;
+    for (int s = 0; s < nsteps; ++s) {
+        const int c = col0 + 32 * s;
+        float pr[32];
+        if (!take(pr)) return false;
+        if (c < p.N) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) pr[j] = pr[j] * (p.alpha * __uint_as_float(r[j]) - sum);
+            store_block_out(p, pm, stage_w, pr, cblk, brows, coff, wrow0, c, min(32, p.N - c));
+        }
+    }
+    return true;
+}
+
 // tmA / tmB map the operands; in pre-split 3xTF32 mode (p.presplit) tmAlo /
 // tmBlo map their lo planes (same layout), which the producer loads next to
 // the raw tiles instead of the split warps computing them.
@@ -871,6 +949,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo,
                       const __grid_constant__ CUtensorMap tmBlo,
+                      const __grid_constant__ CUtensorMap tmP,
                       const __grid_constant__ GemmParams p,
                       const __grid_constant__ PeerMaps pm)
 {
@@ -912,6 +991,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ss->abort_flag = 0;
         ss->tiles_stored = 0u;
         for (int q = 0; q < kEpiWarps / 2; ++q) mbar_init(smem_u32(&ss->pair_bar[q]), 64);
+        for (int q = 0; q < kPRingSlots; ++q) {
+            mbar_init(smem_u32(&ss->p_full[q]), 1);
+            mbar_init(smem_u32(&ss->p_empty[q]), kEpiWarps);
+        }
         mbar_fence_init();
     }
     if (warp == kProducerWarp && lane == 0) {
@@ -922,6 +1005,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_prefetch_map(&tmBlo);
         }
     }
+    if (kRow == kRowSoftmaxBwd && p.p_tma && warp == kExportWarp0 && lane == 0) tma_prefetch_map(&tmP);
     if (warp == kMmaWarp) {
         if (kPair) {
             tmem_alloc_pair(smem_u32(&ss->tmem_base), L::kTmemCols);
@@ -1100,10 +1184,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp >= kExportWarp0) {
+        if (kRow == kRowSoftmaxBwd && p.p_tma) {
+            // -------------------------------------------- P producer (softmax backward)
+            // One lane streams, for every tile of this CTA, its 128 rows of P
+            // into the ring twice (the epilogue's two passes), a step -- the
+            // next 32 columns of both halves -- per slot, in the order the
+            // epilogue warps consume them; plain TMA loads from this GPU's P.
+            if (warp == kExportWarp0 && lane == 0) {
+                uint8_t* ring = reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes +
+                                (size_t)kEpiWarps * kStageFloatsPerWarp * 4;
+                int slot = 0;
+                uint32_t phase = 0, issued = 0, issued_par = 0;
+                bool ok = true;
+                Unit u;
+                for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+                    const TileCoord tc = decode_tile(u.tile, p);
+                    int idx[kMaxBatchDims];
+                    batch_index(tc.batch, p, idx);
+                    int32_t pc[3] = {0, 0, 0};
+                    batch_coords(p, idx, p.p_map, p.p_mult, pc);
+                    const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
+                    for (int step = 0; ok && step < 2 * L::kHalfChunks; ++step) {
+                        const int s = step % L::kHalfChunks;   // both passes walk the same columns
+                        if (!wait_phase<1>(smem_u32(&ss->p_empty[slot]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t fb = smem_u32(&ss->p_full[slot]);
+                        mbar_arrive_expect_tx(fb, kPSlotBytes);
+                        const uint32_t dst = smem_u32(ring + (size_t)slot * kPSlotBytes);
+                        tma_load(&tmP, fb, dst, p.p_rank, 32 * s, m0, pc[0], pc[1], pc[2]);
+                        tma_load(&tmP, fb, dst + kPBoxBytes, p.p_rank, 32 * (L::kHalfChunks + s), m0, pc[0], pc[1],
+                                 pc[2]);
+                        issued |= 1u << slot;
+                        issued_par = (issued_par & ~(1u << slot)) | (phase << slot);
+                        if (++slot == kPRingSlots) { slot = 0; phase ^= 1u; }
+                    }
+                }
+                if (!ok) {
+                    // let every issued copy land before the CTA's shared memory goes away
+                    for (int q = 0; q < kPRingSlots; ++q)
+                        if (issued & (1u << q)) drain_phase(smem_u32(&ss->p_full[q]), (issued_par >> q) & 1u);
+                }
+            }
+            __syncwarp();
+        } else if (p.export_peers && p.npeers > 0) {
         // ------------------------------------------------ export (fused all-gather)
         // Follows the epilogue tile by tile: tile j of this CTA may be copied
         // once all eight epilogue warps have counted it into tiles_stored.
-        if (p.export_peers && p.npeers > 0) {
             const int et = threadIdx.x - kExportWarp0 * 32;
             unsigned int j = 0;
             Unit u;
@@ -1232,6 +1360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr bool softmax_bwd = kRow == kRowSoftmaxBwd;
         uint32_t chunk_phase = 0;
         unsigned int meet_seq = 0;   // row epilogues: meetings with the partner warp so far
+        int p_slot = 0;              // softmax backward with the P ring: the next slot and its phase
+        uint32_t p_phase = 0;
         bool ok = true;
         Unit u;
         for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
@@ -1345,8 +1475,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             } else if constexpr (softmax_bwd) {
                 // fused softmax backward (N <= BN, one n-tile): softmax_bwd_tile
-                if (!softmax_bwd_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, wrow0, cblk, coff,
-                                      stage_w)) {
+                const bool done = p.p_tma
+                    ? softmax_bwd_tile_ring(p, pm, ss, warp, meet_seq, p_slot, p_phase, L::kHalfChunks, t_row,
+                                            c_lo * 32, wrow0, brows, cblk, coff, stage_w)
+                    : softmax_bwd_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, wrow0, cblk, coff,
+                                       stage_w);
+                if (!done) {
                     ok = false;
                     break;
                 }
