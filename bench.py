@@ -52,6 +52,9 @@ def parse_args():
     p.add_argument("--size", type=int, default=SIZE)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="N=1: skip the sub-records (the 8192^3 GEMM in the other mode, and the batched, "
+                        "linear-layer and attention workloads)")
     p.add_argument("--workload", choices=["gemm", "decoder", "batched", "linear", "attention"], default="gemm",
                    help="gemm: the square 8192^3 GEMM (default); decoder: the decoder-only character "
                         "model's training step through the drop-in build, batch-sharded over the GPUs; "
@@ -218,14 +221,20 @@ def main():
         print("size must divide evenly over the ranks", file=sys.stderr)
         return 2
 
-    # CPU baseline first, before any CUDA call in this process.
+    # CPU baselines first, before any CUDA call in this process (the
+    # reference's row-sliced matmul forks worker processes).
     cpu = None
+    small_cpu = {}
+    one_gpu_extras = world == 1 and n == SIZE and not args.no_extras
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = cpu_cores()
         v, kind, used, dt, rows = reference_cpu_sample(n, 8, cores)
         cpu = {"value": v, "unit": UNIT, "cores": used, "kind": kind,
                "sample": f"{rows} rows of A x full B[{n},{n}] ({2.0 * rows * n * n / 1e9:.1f} GFLOP) "
                          f"in {dt:.2f} s over {used} processes"}
+        if one_gpu_extras:
+            for w in ("batched", "linear", "attention"):
+                small_cpu[w] = small_reference_rate(w, 2, 1)
 
     import torch
     import torch.distributed as dist
@@ -398,6 +407,41 @@ def main():
             dist.barrier(device_ids=[local_rank])
             peers_e[1].close()
 
+    # ---- N = 1 sub-records: the same GEMM in the other mode (kernel time),
+    # and the other configurations' workloads (measure_small)
+    extras = None
+    if one_gpu_extras and rank == 0:
+        other = "tf32" if args.mode == "3xtf32" else "3xtf32"
+        _lib.check(lib.mg_set_mode(_lib.MG_MODE_TF32 if other == "tf32" else _lib.MG_MODE_TF32X3))
+        for _ in range(max(3, args.warmup)):
+            gemm()
+        torch.cuda.synchronize()
+        kev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+        oclk = ClockSampler(local_rank)
+        oclk.start()
+        for i in range(args.steps):
+            kev[i][0].record(stream)
+            gemm()
+            kev[i][1].record(stream)
+        torch.cuda.synchronize()
+        oclk_rec = oclk.stop()
+        o_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in kev)
+        bf16_, _, _, src_ = peaks()
+        o_peak = bf16_ / 2.0 / (3.0 if other == "3xtf32" else 1.0)
+        o_tf = 2.0 * n * n * n / (o_ms * 1e-3) / 1e12
+        extras = {other: {"value": o_tf, "unit": UNIT, "ms": o_ms, "mode": other,
+                          "roofline": {"bound": "tensor", "achieved": o_tf, "peak": o_peak, "unit": UNIT,
+                                       "frac": o_tf / o_peak,
+                                       "peak_source": f"{src_} bf16 dense {bf16_:.1f} / 2"
+                                                      + (" / 3" if other == "3xtf32" else "")},
+                          "note": "the same 8192^3 GEMM in the other mode, kernel time (CUDA events), "
+                                  "operands resident, larger than L2", "clocks": oclk_rec}}
+        _lib.check(lib.mg_set_mode(mode))
+        del A, B, C_local, C_full
+        torch.cuda.empty_cache()
+        extras["workloads"] = {w: measure_small(w, args.mode, args.steps, args.warmup, dev, lib, small_cpu.get(w))
+                               for w in ("batched", "linear", "attention")}
+
     if world > 1:
         dist.barrier(device_ids=[local_rank])             # no rank still writes into a peer's C
         if peers is not None:
@@ -442,6 +486,9 @@ def main():
         "exchange_ms": gather_ms if world > 1 else 0.0,
         "clocks": clk,
     }
+    if extras is not None:
+        line["other_mode"] = extras.pop("tf32" if args.mode == "3xtf32" else "3xtf32")
+        line["workloads"] = extras["workloads"]
     print(json.dumps(line), flush=True)
     return 0
 
@@ -563,126 +610,162 @@ def run_small_reference(args):
     return 0
 
 
-def run_small_workload(args):
-    """One-GPU forward + backward GEMM workloads of the matmul path (the
-    parity configurations, timed): every GEMM through the library's public
-    API (functional.py). Each step is timed alone with CUDA events, L2 flushed
-    (a 512 MB write) between steps; GEMM-only time from events around each
-    library call. TFLOP/s against TF32 / 3 (3xTF32) or TF32; the attention
-    score product (HBM-bound) also as GB/s against the measured HBM rate."""
-    if args.impl == "reference":
-        return run_small_reference(args)
+def small_step_calls(workload, dev):
+    """The library calls of one forward + backward step of a one-GPU workload
+    (every GEMM through the public API, functional.py), on seeded synthetic
+    inputs resident in HBM: (flops, config, [(name, fn)]) -- each fn makes
+    one library call and returns its output."""
     import torch
+    from macrograd_b200 import functional as F
 
-    sys.path.insert(0, ROOT)
-    import macrograd_b200 as mg
-    from macrograd_b200 import _lib, functional as F
-
-    rank, local_rank, world = env_rank()
-    if world != 1:
-        print("the small workloads run on one GPU", file=sys.stderr)
-        return 2
-    torch.cuda.set_device(local_rank)
-    dev = torch.device("cuda", local_rank)
-    lib = mg.load()
-    _lib.check(lib.mg_set_mode(_lib.MG_MODE_TF32X3 if args.mode == "3xtf32" else _lib.MG_MODE_TF32))
     g = torch.Generator(device=dev)
     g.manual_seed(20)
-    gemm_events = []
-
-    def timed(fn, *a, **k):
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        r = fn(*a, **k)
-        e1.record()
-        gemm_events.append((e0, e1))
-        return r
-
-    if args.workload == "batched":
+    flops, desc = small_desc(workload)
+    if workload == "batched":
         A = torch.empty(8, 256, 384, device=dev).uniform_(-1, 1, generator=g)
         W = torch.empty(384, 384, device=dev).uniform_(-1, 1, generator=g)
         dC = torch.ones(8, 256, 384, device=dev)
-        flops, desc = small_desc("batched")
-
-        def step():
-            timed(F.matmul, A, W)
-            timed(F.matmul_backward, A, W, dC)
-    elif args.workload == "linear":
+        calls = [("C = A W", lambda: F.matmul(A, W)),
+                 ("dA, dW", lambda: F.matmul_backward(A, W, dC))]
+    elif workload == "linear":
         bound = (6.0 / 384) ** 0.5
         X = torch.empty(16384, 384, device=dev).uniform_(-1, 1, generator=g)
         W = torch.empty(1536, 384, device=dev).uniform_(-bound, bound, generator=g)
         b = torch.empty(1536, device=dev).uniform_(-bound, bound, generator=g)
         dY = torch.empty(16384, 1536, device=dev).normal_(0, 1, generator=g)
-        flops, desc = small_desc("linear")
-
-        def step():
-            timed(F.matmul, X, W, b, False, True)
-            timed(F.matmul_backward, X, W, dY, False, True)   # db = sum(dY) is not a GEMM
+        calls = [("Y = X W^T + b", lambda: F.matmul(X, W, b, False, True)),
+                 ("dX, dW, db", lambda: F.matmul_backward(X, W, dY, False, True, True, (1536,)))]
     else:
         Q = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 0.125, generator=g)
         K = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 0.125, generator=g)
         V = torch.empty(64, 6, 256, 64, device=dev).normal_(0, 1, generator=g)
         dO = torch.ones(64, 6, 256, 64, device=dev)
         Qs = Q * 0.125
-        flops, desc = small_desc("attention")
+        st = {}
+        calls = [("P = softmax(Q K^T / 8 + causal)", lambda: st.__setitem__("P", F.attention_scores(Q, K, 0.125, True))),
+                 ("O = P V", lambda: F.matmul(st["P"], V)),
+                 ("dS = P (dP - rowsum(P dP)), dP = dO V^T",
+                  lambda: st.__setitem__("dS", F.attention_softmax_backward(dO, V, st["P"]))),
+                 ("dV = P^T dO", lambda: F.matmul(st["P"], dO, None, True, False)),
+                 ("dQ/8 = dS K", lambda: F.matmul(st["dS"], K)),
+                 ("dK = dS^T Q/8", lambda: F.matmul(st["dS"], Qs, None, True, False))]
+    return flops, desc, calls
 
-        def step():
-            P = timed(F.attention_scores, Q, K, 0.125, True)
-            timed(F.matmul, P, V)
-            dS = timed(F.attention_softmax_backward, dO, V, P)
-            timed(F.matmul, P, dO, None, True, False)
-            timed(F.matmul, dS, K)
-            timed(F.matmul, dS, Qs, None, True, False)
 
+def measure_small(workload, mode, steps, warmup, dev, lib, cpu=None):
+    """Times one workload's step on this GPU. Every library call is captured
+    in a CUDA graph of its own (the launch-bound small calls pay no host
+    overhead) and the graphs are replayed back to back between CUDA events on
+    the launching stream, L2 flushed before every step (a 512 MB write,
+    untimed): per-call device times, their sum the step's GEMM time. The same
+    step run eagerly through the Python API is timed beside it. Returns the
+    workload's record (TFLOP/s against TF32 / 3 or TF32; HBM rate of the
+    attention score product and of its fused softmax backward)."""
+    import torch
+    from macrograd_b200 import _lib
+
+    _lib.check(lib.mg_set_mode(_lib.MG_MODE_TF32X3 if mode == "3xtf32" else _lib.MG_MODE_TF32))
+    flops, desc, calls = small_step_calls(workload, dev)
     flush = torch.empty(128 * 1024 * 1024, device=dev)
-    for _ in range(max(3, args.warmup)):
-        step()
+    for _ in range(max(3, warmup)):
+        for _, fn in calls:
+            fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs = []
+    for _, fn in calls:
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=side):
+            fn()
+        graphs.append(gr)
+    torch.cuda.synchronize()
+    for gr in graphs:
+        gr.replay()
     torch.cuda.synchronize()
     launches0 = lib.mg_launch_count()
-    clocks = ClockSampler(local_rank)
+    clocks = ClockSampler(dev.index or 0)
     clocks.start()
-    step_ms, gemm_ms, score_ms, each_ms = [], [], [], []
-    for _ in range(args.steps):
+    each_ms = []
+    for _ in range(steps):
         flush.fill_(1.0)
-        gemm_events.clear()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(graphs) + 1)]
+        ev[0].record()
+        for i, gr in enumerate(graphs):
+            gr.replay()
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        each_ms.append([ev[i].elapsed_time(ev[i + 1]) for i in range(len(graphs))])
+    eager_ms = []
+    for _ in range(steps):
+        flush.fill_(1.0)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        step()
+        for _, fn in calls:
+            fn()
         e1.record()
         torch.cuda.synchronize()
-        step_ms.append(e0.elapsed_time(e1))
-        gemm_ms.append(sum(a.elapsed_time(b) for a, b in gemm_events))
-        score_ms.append(gemm_events[0][0].elapsed_time(gemm_events[0][1]))
-        each_ms.append([a.elapsed_time(b) for a, b in gemm_events])
+        eager_ms.append(e0.elapsed_time(e1))
     clk = clocks.stop()
-    launches = lib.mg_launch_count() - launches0
-    ms = statistics.mean(step_ms)
-    gms = statistics.mean(gemm_ms)
+    # graph replays make no library call: the eager steps give the kernels per step
+    launches = (lib.mg_launch_count() - launches0) // max(1, steps)
+    per_call = [statistics.mean(x) for x in zip(*each_ms)]
+    gms = sum(per_call)
     bf16, _, hbm, src = peaks()
-    peak = bf16 / 2.0 / (3.0 if args.mode == "3xtf32" else 1.0)
-    line = {
-        "metric": f"{args.workload} fwd+bwd GEMM TFLOP/s", "value": flops / (gms * 1e-3) / 1e12, "unit": "TFLOP/s",
-        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "gemm_ms_per_step": gms,
-        "step_tflops": flops / (ms * 1e-3) / 1e12, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (torch generator, seeded)",
-        "config": {**desc, "mode": args.mode, "gflop_per_step": flops / 1e9,
-                   "l2": "flushed between steps (512 MB write, untimed)"},
-        "roofline": {"bound": "tensor", "achieved": flops / (gms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
-                     "frac": flops / (gms * 1e-3) / 1e12 / peak,
-                     "peak_source": f"{src} bf16 dense {bf16:.1f} / 2" + (" / 3" if args.mode == "3xtf32" else "")},
-        "gpu_launches": int(launches),
+    peak = bf16 / 2.0 / (3.0 if mode == "3xtf32" else 1.0)
+    tf = flops / (gms * 1e-3) / 1e12
+    rec = {
+        "metric": f"{workload} fwd+bwd GEMM TFLOP/s", "value": tf, "unit": "TFLOP/s", "mode": mode,
+        "gemm_ms_per_step": gms, "eager_ms_per_step": statistics.mean(eager_ms),
+        "config": {**desc, "mode": mode, "gflop_per_step": flops / 1e9,
+                   "l2": "flushed before every step (512 MB write, untimed)",
+                   "timing": "each library call captured in its own CUDA graph, replayed back to back between "
+                             "CUDA events (device time); eager_ms_per_step: the same step through the Python API"},
+        "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                     "peak_source": f"{src} bf16 dense {bf16:.1f} / 2" + (" / 3" if mode == "3xtf32" else "")},
+        "per_call_ms": dict(zip([n for n, _ in calls], per_call)),
+        "gpu_launches_per_step": int(launches),
         "clocks": clk,
-        "per_call_ms": [statistics.mean(x) for x in zip(*each_ms)],
-        "cpu_baseline": None if args.no_cpu_baseline else small_reference_rate(args.workload, 3, 1),
+        "cpu_baseline": cpu,
     }
-    if args.workload == "attention":
-        sbytes = 4.0 * (2 * 64 * 6 * 256 * 64 + 64 * 6 * 256 * 256)
-        sms = statistics.mean(score_ms)
-        line["score_product"] = {"bound": "hbm", "ms": sms, "achieved": sbytes / (sms * 1e-3) / 1e9, "peak": hbm,
-                                 "unit": "GB/s", "frac": sbytes / (sms * 1e-3) / 1e9 / hbm,
-                                 "bytes": sbytes, "note": "Q, K read + P written, one fused launch"}
+    if workload == "attention":
+        L, nbh = 256, 64 * 6
+        sbytes = 4.0 * nbh * (2 * L * 64 + L * L)            # Q, K read; P written
+        bbytes = 4.0 * nbh * (2 * L * 64 + 2 * L * L)        # dO, V, P read; dS written
+        for key, i, b, what in (("score_product", 0, sbytes, "Q, K read + P written, one fused launch"),
+                                ("softmax_backward", 2, bbytes, "dO, V, P read + dS written, one fused launch")):
+            ms = per_call[i]
+            rec[key] = {"bound": "hbm", "ms": ms, "achieved": b / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                        "frac": b / (ms * 1e-3) / 1e9 / hbm, "bytes": b, "note": what}
+    del graphs
+    torch.cuda.synchronize()
+    return rec
+
+
+def run_small_workload(args):
+    """One-GPU forward + backward GEMM workloads of the matmul path (the
+    parity configurations, timed) as their own JSON line: measure_small."""
+    if args.impl == "reference":
+        return run_small_reference(args)
+    rank, local_rank, world = env_rank()
+    if world != 1:
+        print("the small workloads run on one GPU", file=sys.stderr)
+        return 2
+    cpu = None if args.no_cpu_baseline else small_reference_rate(args.workload, 3, 1)   # before any CUDA call
+    import torch
+
+    sys.path.insert(0, ROOT)
+    import macrograd_b200 as mg
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    lib = mg.load()
+    rec = measure_small(args.workload, args.mode, args.steps, args.warmup, dev, lib, cpu)
+    line = {"metric": rec.pop("metric"), "value": rec.pop("value"), "unit": rec.pop("unit"), "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": rec["gemm_ms_per_step"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (torch generator, seeded), resident in HBM", **rec}
     print(json.dumps(line), flush=True)
     return 0
 

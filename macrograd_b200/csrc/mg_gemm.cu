@@ -549,10 +549,14 @@ mg_status relayout_operand(Operand& x, int nbd, const int32_t* bsize, Workspace&
 int tuning_int(const char* name, int dflt, int lo, int hi);
 
 // K split of the last partial wave (mg_plan.h): MG_GEMM_SPLIT=0 turns it off,
-// MG_GEMM_SPLIT_MIN_KB sets the shortest range in K-blocks (default 16).
+// MG_GEMM_SPLIT_MIN_KB sets the shortest range in K-blocks: by default 16, or
+// 4 for a launch of less than half a wave (e.g. 16 tiles of a batched
+// [8, 256, 384] product on 74 SM pairs), whose few tiles would otherwise run
+// their whole K one stage after another while most SMs idle.
 int plan_split(mg::GemmParams& gp, int units)
 {
-    const int min_kb = tuning_int("MG_GEMM_SPLIT", 1, 0, 1) ? tuning_int("MG_GEMM_SPLIT_MIN_KB", 16, 1, 1 << 20) : 0;
+    const int dflt = 2 * (int64_t)gp.total_tiles <= units ? 4 : 16;
+    const int min_kb = tuning_int("MG_GEMM_SPLIT", 1, 0, 1) ? tuning_int("MG_GEMM_SPLIT_MIN_KB", dflt, 1, 1 << 20) : 0;
     return mg::plan_k_split(gp.plan, gp.total_tiles, units, gp.num_kb, min_kb);
 }
 
@@ -748,13 +752,26 @@ int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, const DeviceStat
     return cost(224) < cost(256) ? 224 : 256;
 }
 
-bool use_pair(int M)
+// The SM-pair kernel for output matrices of more than 128 rows -- it halves
+// the B tile each SM loads and keeps more stages in flight, which large GEMMs
+// need -- except for many small matrices (at most 256 rows each, e.g. the
+// per-head products of attention) whose single-SM tiles fill at least a wave:
+// there the pair's cross-SM hand-off per stage costs more than it saves
+// (measured on the attention products: 0.066 vs 0.079 ms for P V). The fused
+// softmax backward wider than 128 columns in 3xTF32 stays on pairs, whose
+// shared memory has room for its P ring beside two operand stages.
+bool use_pair(const mg_gemm_desc* d, int64_t nbatch, int sm_count, int32_t mode)
 {
     if (const char* e = std::getenv("MG_GEMM_PAIR")) {
         if (e[0] == '0') return false;
         if (e[0] == '1') return true;
     }
-    return M > mg::kBM;
+    if (d->M <= mg::kBM) return false;
+    if (d->M <= 2 * mg::kBM && nbatch * ((d->M + mg::kBM - 1) / mg::kBM) >= sm_count) {
+        const bool wide_bwd = (d->epilogue & mg::kEpiSoftmaxBwd) && d->N > 128 && mode == MG_MODE_TF32X3;
+        if (!wide_bwd) return false;
+    }
+    return true;
 }
 
 mg_status validate(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias)
@@ -930,7 +947,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
             return fail(MG_ERR_UNSUPPORTED, "operand B cannot be mapped for TMA");
     }
 
-    const bool pair = use_pair(d->M);
+    const bool pair = use_pair(d, nbatch, dev->sm_count, mode);
     const int bn = choose_bn(d, pair, nbatch, dev);
     const int tile_rows = pair ? 2 * mg::kBM : mg::kBM;   // output rows per tile
     const int b_rows = pair ? bn / 2 : bn;                // B rows (N) one CTA loads
@@ -1407,7 +1424,9 @@ static mg_status scatter_by_bands(const mg_gemm_desc* d, const float* A, const f
     if (s != MG_OK) return s;
     s = copy_engine_state(dev);
     if (s != MG_OK) return s;
-    const bool pair = use_pair(d->M);
+    // the same choice gemm_impl makes for each band (one matrix, the rank's rows)
+    const int32_t mode = d->mode == MG_MODE_DEFAULT ? resolve_default_mode() : d->mode;
+    const bool pair = use_pair(d, 1, dev->sm_count, mode);
     const int tile_rows = pair ? 2 * mg::kBM : mg::kBM;
     const int m_tiles = (int)((d->M + tile_rows - 1) / tile_rows);
     const int n_tiles = (int)((d->N + 255) / 256);

@@ -120,7 +120,7 @@ int main()
     int nsplit = 0;
     const int units[] = {1, 2, 3, 37, 74, 148};
     const int kbs[] = {1, 8, 12, 32, 256};
-    const int mks[] = {1, 16};
+    const int mks[] = {1, 4, 16};
     for (int T = 1; T < 320; ++T)
         for (int U : units)
             for (int KB : kbs)
