@@ -9,6 +9,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <nvtx3/nvToolsExt.h>
 
 #include <algorithm>
 #include <atomic>
@@ -86,6 +87,16 @@ bool ipc_imported(const void* p)
     }
     return false;
 }
+
+// NVTX range around a C-ABI entry point, so that profiler timelines show the
+// library's calls (header-only NVTX: without an attached tool a range costs a
+// check of a function pointer).
+struct NvtxRange {
+    explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange&) = delete;
+    NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 mg_status fail(mg_status s, const char* fmt, ...)
 {
@@ -593,7 +604,7 @@ bool setup_split(mg::GemmParams& gp, int units, Workspace* ws, cudaStream_t st, 
 
 template <int BN, bool kPair, int kRow>
 mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& malo,
-                    const CUtensorMap& mblo, const CUtensorMap& mp, mg::GemmParams& gp, const mg::PeerMaps& pm,
+                    const CUtensorMap& mblo, const CUtensorMap& mp, const CUtensorMap& mc, mg::GemmParams& gp, const mg::PeerMaps& pm,
                     cudaStream_t st, Workspace* ws, bool allow_split)
 {
     using L = mg::Layout<BN, kPair>;
@@ -648,7 +659,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             cfg.attrs = attr2;
             cfg.numAttrs = 2;
             cfg.gridDim = dim3((unsigned)(2 * resident), 1, 1);
-            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, gp, pm) == cudaSuccess) {
+            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, mc, gp, pm) == cudaSuccess) {
                 g_launches++;
                 return MG_OK;
             }
@@ -662,7 +673,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         }
         const int pairs = std::max(1, std::min(gp.total_tiles, resident));
         cfg.gridDim = dim3((unsigned)(2 * pairs), 1, 1);
-        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, gp, pm));
+        MG_CUDA_TRY(cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, mc, gp, pm));
     } else {
         const bool split_k = setup_split<BN>(gp, dev->sm_count, ws, st, allow_split);
         gp.dbuf = (!split_k && gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
@@ -677,7 +688,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             attr[0].val.cooperative = 1;
             cfg.attrs = attr;
             cfg.numAttrs = 1;
-            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, gp, pm) == cudaSuccess) {
+            if (cudaLaunchKernelEx(&cfg, k, ma, mb, malo, mblo, mp, mc, gp, pm) == cudaSuccess) {
                 g_launches++;
                 return MG_OK;
             }
@@ -688,7 +699,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
             gp.dbuf = (gp.num_kb <= gp.chunk_kb && tuning_int("MG_GEMM_DBUF", 1, 0, 1)) ? 1 : 0;
         }
         const int grid = std::max(1, std::min(gp.total_tiles, dev->sm_count));
-        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, mp, gp, pm);
+        k<<<grid, mg::kThreads, smem, st>>>(ma, mb, malo, mblo, mp, mc, gp, pm);
         MG_CUDA_TRY(cudaGetLastError());
     }
     g_launches++;
@@ -1032,6 +1043,25 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.ldc = d->ldc;
     gp.bias = has_bias ? bias : nullptr;
     gp.aux = aux;
+    // output blocks by TMA tensor stores where C allows a map (16-byte row
+    // pitch and batch strides, aligned base) and is only written (beta 0, no
+    // rows to other ranks): the epilogue warps go on while the writes drain
+    CUtensorMap mc = ma;
+    if (!scatter && d->beta == 0.f && tuning_int("MG_GEMM_C_TMA", 1, 0, 1)) {
+        Operand cx{C, d->M, d->N, d->ldc, {0}};
+        for (int i = 0; i < nbd; ++i) cx.bs[i] = d->c_batch_stride[i];
+        BatchMap cbm;
+        if (build_batch_map(nbd, d->batch, cx.bs, &cbm) && tma_compatible(cx, cbm)) {
+            s = encode_map(&mc, cx, cbm, 0, 32);
+            if (s != MG_OK) return s;
+            gp.c_tma = 1;
+            gp.c_rank = 2 + cbm.nmap;
+            for (int i = 0; i < mg::kMaxBatchDims; ++i) {
+                gp.c_map[i] = cbm.map[i];
+                gp.c_mult[i] = cbm.mult[i];
+            }
+        }
+    }
     // softmax backward: P (laid out like C) streamed by TMA into the epilogue's
     // ring, where its layout allows a tensor map (16-byte row pitch and batch
     // strides, aligned base); otherwise the epilogue reads it directly
@@ -1058,6 +1088,12 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.beta = d->beta;
     gp.epi = d->epilogue;
     gp.status = dev->status;
+    // bounded waits: 4 s, unless shortened (MG_GEMM_WAIT_LIMIT_MS, 1..4000);
+    // MG_GEMM_TEST_STALL=1 withholds every CTA's second K-block so that a test
+    // can watch a wait run out and the kernel report it (mg_device_status)
+    const int limit_ms = (int)(mg::kWaitLimitNs / 1000000ull);
+    gp.wait_limit_ns = (uint64_t)tuning_int("MG_GEMM_WAIT_LIMIT_MS", limit_ms, 1, limit_ms) * 1000000ull;
+    gp.test_stall = tuning_int("MG_GEMM_TEST_STALL", 0, 0, 1);
     mg::PeerMaps pm;
     std::memset(&pm, 0, sizeof(pm));
     // Export mode (default): the epilogue writes this GPU's own full C and the
@@ -1065,7 +1101,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     // epilogue never waits on NVLink. Needs one destination in this process's
     // own memory (not mapped from another rank).
     int local = -1;
-    if (scatter && tuning_int("MG_GEMM_EXPORT", 1, 0, 2) != 0) {
+    if (scatter && tuning_int("MG_GEMM_EXPORT", 1, 0, 2) != 0) {   // (a 2 that reached here: export warps)
         for (int q = 0; q < scatter->npeers && local < 0; ++q)
             if (!ipc_imported(scatter->peers[q])) local = q;
     }
@@ -1113,7 +1149,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const bool allow_split = row == mg::kRowNone;
     auto go = [&](auto bn_c, auto pair_c, auto row_c) {
         return launch_tc<decltype(bn_c)::value, decltype(pair_c)::value, decltype(row_c)::value>(
-            dev, ma, mb, malo, mblo, mp, gp, pm, st, &ws, allow_split);
+            dev, ma, mb, malo, mblo, mp, mc, gp, pm, st, &ws, allow_split);
     };
     using T = std::true_type;
     using F = std::false_type;
@@ -1141,6 +1177,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
 mg_status mg_gemm(const mg_gemm_desc* d, float* C, const float* A, const float* B, const float* bias,
                   void* stream)
 {
+    NvtxRange nvtx_range("mg_gemm");
     return gemm_impl(d, C, A, B, bias, stream, nullptr, 0);
 }
 
@@ -1214,6 +1251,7 @@ mg_status mg_matmul(float* out, const float* A, const float* B, const int32_t* o
                     const int32_t* A_shape, const int32_t* B_shape, int32_t rank, int32_t trans_a,
                     int32_t trans_b, void* stream)
 {
+    NvtxRange nvtx_range("mg_matmul");
     g_last_error.clear();
     mg_gemm_desc d;
     mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, nullptr, rank, trans_a, trans_b);
@@ -1226,6 +1264,7 @@ mg_status mg_matmul_bias(float* out, const float* A, const float* B, const float
                          const int32_t* bias_shape, int32_t rank, int32_t trans_a, int32_t trans_b,
                          void* stream)
 {
+    NvtxRange nvtx_range("mg_matmul_bias");
     g_last_error.clear();
     if (!bias_shape) return fail(MG_ERR_INVALID, "bias_shape is NULL");
     mg_gemm_desc d;
@@ -1239,6 +1278,7 @@ mg_status mg_matmul_accumulate(float* out, const float* A, const float* B, const
                                const int32_t* A_shape, const int32_t* B_shape, int32_t rank, int32_t trans_a,
                                int32_t trans_b, float beta, void* stream)
 {
+    NvtxRange nvtx_range("mg_matmul_accumulate");
     g_last_error.clear();
     if (beta != 0.f && beta != 1.f) return fail(MG_ERR_INVALID, "beta must be 0 or 1 (got %g)", (double)beta);
     mg_gemm_desc d;
@@ -1251,6 +1291,7 @@ mg_status mg_matmul_accumulate(float* out, const float* A, const float* B, const
 mg_status mg_sum_into(float* dst, const float* src, const int32_t* dst_shape, const int32_t* src_shape,
                       int32_t rank, float beta, void* stream)
 {
+    NvtxRange nvtx_range("mg_sum_into");
     g_last_error.clear();
     if (!dst_shape || !src_shape) return fail(MG_ERR_INVALID, "shape pointer is NULL");
     if (rank < 1 || rank > MG_MAX_BATCH_DIMS + 2)
@@ -1351,6 +1392,7 @@ mg_status mg_matmul_softmax(float* out, const float* A, const float* B, const fl
                             const int32_t* bias_shape, int32_t rank, int32_t trans_a, int32_t trans_b,
                             float alpha, int32_t causal, void* stream)
 {
+    NvtxRange nvtx_range("mg_matmul_softmax");
     g_last_error.clear();
     mg_gemm_desc d;
     mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, bias ? bias_shape : nullptr, rank,
@@ -1366,6 +1408,7 @@ mg_status mg_matmul_softmax_backward(float* dS, const float* A, const float* B, 
                                      const int32_t* out_shape, const int32_t* A_shape, const int32_t* B_shape,
                                      int32_t rank, int32_t trans_a, int32_t trans_b, float alpha, void* stream)
 {
+    NvtxRange nvtx_range("mg_matmul_softmax_backward");
     g_last_error.clear();
     if (!P) return fail(MG_ERR_INVALID, "P is NULL");
     mg_gemm_desc d;
@@ -1388,6 +1431,7 @@ mg_status mg_matmul_noalloc(float* out, const float* A, const float* B, const in
                             const int32_t* A_shape, const int32_t* B_shape, int32_t rank,
                             int32_t trans_a, int32_t trans_b, void* stream)
 {
+    NvtxRange nvtx_range("mg_matmul_noalloc");
     g_last_error.clear();
     mg_gemm_desc d;
     mg_status s = seam_desc(&d, out_shape, A_shape, B_shape, nullptr, rank, trans_a, trans_b);
@@ -1480,6 +1524,7 @@ mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const floa
                                float* const* peer_C, int32_t npeers, int64_t row0, int64_t rows_full,
                                void* stream)
 {
+    NvtxRange nvtx_range("mg_gemm_scatter_rows");
     g_last_error.clear();
     if (!d) return fail(MG_ERR_INVALID, "descriptor is NULL");
     if (npeers < 1 || npeers > mg::kMaxPeers)
@@ -1499,8 +1544,12 @@ mg_status mg_gemm_scatter_rows(const mg_gemm_desc* d, const float* A, const floa
     }
     if (d->K == 0) return fail(MG_ERR_UNSUPPORTED, "K = 0 is not supported by the scattering GEMM");
     // copy engines instead of the kernel's export warps: a 2-D C without a
-    // row epilogue (bands cut the rows), one destination in this process
-    if (tuning_int("MG_GEMM_EXPORT", 1, 0, 2) == 2 && d->batch_rank == 0 &&
+    // row epilogue (bands cut the rows), one destination in this process. By
+    // default for jobs of 4 ranks, where it measured fastest (8192^3 over 4
+    // B200s: 772 TFLOP/s against 730 for the export warps and 663 for NCCL;
+    // with 2 and 8 ranks the export warps led: 427 / 1134 against 411 / 979)
+    const int export_dflt = npeers == 4 ? 2 : 1;
+    if (tuning_int("MG_GEMM_EXPORT", export_dflt, 0, 2) == 2 && d->batch_rank == 0 &&
         (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) == 0) {
         int local = -1;
         for (int q = 0; q < npeers && local < 0; ++q)

@@ -497,15 +497,16 @@ def test_config3_attention_forward_and_backward():
 
 @pytest.mark.parametrize("mode", MODES)
 def test_config4_square_8192_row_slices(mode):
-    """A,B[8192,8192] ~ U(-1,1) seed 4; rows 0..31 and 4096..4127 of C against
-    the oracle on the same row slices (bit-identical to its full product)."""
+    """A,B[8192,8192] ~ U(-1,1) seed 4; rows 0..31, 4096..4127 and the last
+    m-tile's 8160..8191 (the last wave's tiles) of C against the oracle on the
+    same row slices (bit-identical to its full product)."""
     set_mode(mode)
     n = 8192
     A = ob.seeded_uniform((n, n), 4)
     B = ob.seeded_uniform((n, n), 1004)
     C = F.matmul(cuda(A), cuda(B))
     torch.cuda.synchronize()
-    for r0 in (0, 4096):
+    for r0 in (0, 4096, 8160):
         rows = slice(r0, r0 + 32)
         got = C[rows].cpu().numpy()
         assert_close(got, ob.oracle_matmul(A[rows], B), mode, f"cfg4 rows {r0}")
