@@ -93,7 +93,7 @@ constexpr int kPRingSlots = 2;
 constexpr uint32_t kPBoxBytes = 128u * 128u;
 constexpr uint32_t kPSlotBytes = 2u * kPBoxBytes;
 constexpr int kMaxPeers = 8;
-constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s: far above any legitimate wait
+constexpr uint64_t kWaitLimitNs = 4000000000ull;   // 4 s, the default limit: far above any legitimate wait
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // 200 ms for draining after an abort
 constexpr uint32_t kSleepHintNs = 20000u;          // try_wait suspend hint
 
@@ -144,6 +144,10 @@ struct GemmParams {
     int64_t c_bs[kMaxBatchDims];
     const float* bias;
     const float* aux;           // kEpiSoftmaxBwd: the softmax output P, laid out like C
+    int c_tma;                  // output blocks leave by TMA tensor stores (map tmC): beta 0, C mappable
+    int c_rank;                 // tmC's rank (2 + mapped batch dims)
+    int8_t c_map[kMaxBatchDims];
+    int32_t c_mult[kMaxBatchDims];
     int p_tma;                  // kEpiSoftmaxBwd: P streamed by TMA (map tmP) into the P ring
     int p_rank;                 // tmP's rank (2 + mapped batch dims)
     int8_t p_map[kMaxBatchDims];
@@ -153,6 +157,8 @@ struct GemmParams {
     float alpha, beta;
     int epi;
     int* status;                // device status word pair {code, detail}
+    uint64_t wait_limit_ns;     // limit of every bounded wait (kWaitLimitNs unless a test shortens it)
+    int test_stall;             // failure-path test: each CTA's producer stops after its first K-block
     // Fused all-gather of a row-sharded GEMM: when npeers > 0, every output
     // row chunk is written to each peers[q] (the full C of every rank, this
     // rank's own included) at row peer_row0 + m instead of to C.
@@ -309,7 +315,7 @@ __device__ __forceinline__ bool wait_phase(uint32_t bar, uint32_t parity, Shared
                 if (test()) return true;
         }
         if (ss->abort_flag) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > p.wait_limit_ns) {
             record_failure(p, ss, where);
             return false;
         }
@@ -364,27 +370,64 @@ __host__ __device__ constexpr int batch_of(int n, int b = 16)
     return (b <= 1 || n % b == 0) ? (b < 1 ? 1 : b) : batch_of(n, b - 1);
 }
 
-// Warp-collective store of a 32 x 32 output block. The TMEM layout gives each
-// lane one row (v[j] = column gn0 + j of row block_row0 + lane); written as
-// is, one warp store touches 32 rows at 16 bytes each, which is expensive over
-// NVLink. The block is therefore staged in shared memory (16-byte chunks
-// XOR-swizzled by row: conflict-free both ways) and written back
-// row-contiguous: each warp store covers 4 rows x 128 bytes. Destinations: C
-// (`blk` = the block's first row there, `rows` of its 32 rows inside the
-// matrix), or with a fused all-gather every rank's full C. All 32 lanes must
-// call it.
+// A warp's 32-row block of the output tile: its first row in C (`blk`; in
+// export mode this GPU's full C, at this rank's row offset), how many of its
+// rows are inside the matrix, its first row within the batch's matrix, the
+// batch's element offset in C, and -- for TMA stores -- C's map and the
+// batch's map coordinates.
+struct OutRows {
+    float* blk;
+    int rows;
+    int row0;
+    int64_t coff;
+    const CUtensorMap* map;
+    int32_t cc[3];
+};
+
+// Before a warp writes its staging block: with TMA stores, the previous
+// store's read of the block must be over (the write of C itself may still be
+// in flight -- that is the point). Warp-collective.
+__device__ __forceinline__ void staging_free(const GemmParams& p)
+{
+    if (p.c_tma) {
+        if ((threadIdx.x & 31) == 0) bulk_wait_read_all();
+        __syncwarp();
+    }
+}
+
+// Warp-collective store of a 32 x 32 output block (v[j] = column gn0 + j of
+// row row0 + lane). The TMEM layout gives each lane one row; written as is,
+// one warp store would touch 32 rows at 16 bytes each. The block is staged in
+// shared memory instead -- 16-byte chunks XOR-swizzled by row, conflict-free
+// both ways, which is also the 128-byte-swizzled layout of a TMA {32, 32} box
+// -- and then (a) handed to the TMA engine as one tensor store into C
+// (p.c_tma: the warp moves on while the write drains), (b) handed to it once
+// per rank for a fused all-gather (p.peer_tma), or (c) written back
+// row-contiguous by the warp, each store 4 rows x 128 bytes, into C or every
+// rank's C. All 32 lanes must call it.
 __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerMaps& pm, float* stage,
-                                                const float* v, float* blk, int rows, int64_t coff, int block_row0,
-                                                int gn0, int nvalid)
+                                                const float* v, const OutRows& o, int gn0, int nvalid)
 {
     const int lane = threadIdx.x & 31;
+    staging_free(p);
 #pragma unroll
     for (int q = 0; q < 8; ++q)
         reinterpret_cast<float4*>(stage + lane * 32)[q ^ (lane & 7)] =
             make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    if (p.c_tma) {
+        // rows past M and columns past N are clipped by the map
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && o.rows > 0) {   // (a block wholly past M stores nothing)
+            tma_store(o.map, smem_u32(stage), p.c_rank, gn0, o.row0, o.cc[0], o.cc[1], o.cc[2]);
+            bulk_commit_group();
+        }
+        __syncwarp();
+        return;
+    }
     __syncwarp();
     const bool to_peers = p.npeers > 0 && !p.export_peers;   // the epilogue itself writes every rank's C
-    if (to_peers && p.peer_tma && block_row0 + 32 <= p.M) {
+    if (to_peers && p.peer_tma && o.row0 + 32 <= p.M) {
         // The staging block is laid out as a TMA 128B-swizzled {32, 32} box:
         // hand it to the TMA engine once per destination (columns past N are
         // clipped by the map), and wait only until it has been read.
@@ -393,7 +436,7 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
         if (lane == 0) {
             const uint32_t src = smem_u32(stage);
             for (int q = 0; q < p.npeers; ++q)
-                tma_store_2d(&pm.m[q], src, gn0, (int32_t)(p.peer_row0 + block_row0));
+                tma_store_2d(&pm.m[q], src, gn0, (int32_t)(p.peer_row0 + o.row0));
             bulk_commit_group();
             bulk_wait_read_all();
         }
@@ -412,12 +455,12 @@ __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerM
     }
 #pragma unroll 1
     for (int dsti = 0; dsti < ndst; ++dsti) {
-        float* base = to_peers ? p.peers[dsti] + coff + (p.peer_row0 + block_row0) * p.ldc : blk;
+        float* base = to_peers ? p.peers[dsti] + o.coff + (p.peer_row0 + o.row0) * p.ldc : o.blk;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = i * 4 + r_lane;
             const float4 val = vals[i];
-            if (r >= rows || 4 * q >= nvalid) continue;
+            if (r >= o.rows || 4 * q >= nvalid) continue;
             float* dst = base + (int64_t)r * p.ldc + gn0 + 4 * q;
             if (4 * q + 4 <= nvalid && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
                 *reinterpret_cast<float4*>(dst) = val;
@@ -443,7 +486,7 @@ __device__ __forceinline__ bool wait_count(const unsigned int* ctr, unsigned int
         __nanosleep(1000);
         if (*c >= target) return true;
         if (ss->abort_flag) return false;
-        if (global_timer_ns() - t0 > kWaitLimitNs) {
+        if (global_timer_ns() - t0 > p.wait_limit_ns) {
             record_failure(p, ss, where);
             return false;
         }
@@ -770,16 +813,17 @@ __device__ __forceinline__ float softmax_bwd_rowsum(uint32_t t_row, int c0, int 
 // half, columns [c0, c1), stored like any output block.
 __device__ __forceinline__ void softmax_bwd_out(const GemmParams& p, const PeerMaps& pm, uint32_t t_row, int c0, int c1,
                                              const float* pblk, int rows, bool vec, float* stage, float sum,
-                                             float* cblk, int64_t coff, int wrow0)
+                                             const OutRows& o)
 {
     for (int c = c0; c < c1; c += 32) {
         float pr[32];
+        staging_free(p);
         load_row_block(pblk + c, p.ldc, rows, p.N - c, vec, stage, pr);
         uint32_t r[32];
         tmem_ld32(t_row + c, r);
 #pragma unroll
         for (int j = 0; j < 32; ++j) pr[j] = pr[j] * (p.alpha * __uint_as_float(r[j]) - sum);
-        store_block_out(p, pm, stage, pr, cblk, rows, coff, wrow0, c, min(32, p.N - c));
+        store_block_out(p, pm, stage, pr, o, c, min(32, p.N - c));
     }
 }
 
@@ -795,10 +839,11 @@ __device__ __forceinline__ void softmax_bwd_out(const GemmParams& p, const PeerM
 // reciprocal). Returns false when a meeting gave up (abort). Out of line: one
 // call per tile keeps the main epilogue loop's registers free.
 __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps& pm, SharedState* ss, int warp,
-                                          unsigned int& meet_seq, uint32_t t_row, int col0, int col1, int wrow0,
-                                          int gm, const float* bias_row, float* cblk, int brows, int64_t coff,
-                                          float* stage_w)
+                                          unsigned int& meet_seq, uint32_t t_row, int col0, int col1, int gm,
+                                          const float* bias_row, const OutRows& o, float* stage_w)
 {
+    const int wrow0 = o.row0;
+    staging_free(p);   // the posts below go into the staging block
     const int lane = threadIdx.x & 31;
     const int half = warp >> 2;
     const bool causal = (p.epi & kEpiCausal) != 0;
@@ -837,7 +882,7 @@ __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = dead;
         }
-        store_block_out(p, pm, stage_w, v, cblk, brows, coff, wrow0, c, min(32, p.N - c));
+        store_block_out(p, pm, stage_w, v, o, c, min(32, p.N - c));
     }
     return true;
 }
@@ -849,9 +894,12 @@ __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps
 // (load_row_block). The two column halves of a row meet like the forward
 // softmax's. Arguments as softmax_tile.
 __device__ __forceinline__ bool softmax_bwd_tile(const GemmParams& p, const PeerMaps& pm, SharedState* ss, int warp,
-                                              unsigned int& meet_seq, uint32_t t_row, int col0, int col1, int wrow0,
-                                              float* cblk, int64_t coff, float* stage_w)
+                                              unsigned int& meet_seq, uint32_t t_row, int col0, int col1,
+                                              const OutRows& o, float* stage_w)
 {
+    const int wrow0 = o.row0;
+    const int64_t coff = o.coff;
+    staging_free(p);
     const int lane = threadIdx.x & 31;
     const int half = warp >> 2;
     float* xch = stage_w;
@@ -865,7 +913,7 @@ __device__ __forceinline__ bool softmax_bwd_tile(const GemmParams& p, const Peer
     if (!pair_meet(ss, warp, meet_seq, p)) return false;
     sum = half ? pxch[lane] + sum : sum + pxch[lane];   // first half's columns first
     if (!pair_meet(ss, warp, meet_seq, p)) return false;
-    softmax_bwd_out(p, pm, t_row, col0, c1, pblk, wrows, pvec, stage_w, sum, cblk, coff, wrow0);
+    softmax_bwd_out(p, pm, t_row, col0, c1, pblk, wrows, pvec, stage_w, sum, o);
     return true;
 }
 
@@ -877,9 +925,10 @@ __device__ __forceinline__ bool softmax_bwd_tile(const GemmParams& p, const Peer
 // the warp has its rows; `slot` / `phase` follow the ring across tiles.
 __device__ __forceinline__ bool softmax_bwd_tile_ring(const GemmParams& p, const PeerMaps& pm, SharedState* ss,
                                                    int warp, unsigned int& meet_seq, int& slot, uint32_t& phase,
-                                                   int nsteps, uint32_t t_row, int col0, int wrow0, int brows,
-                                                   float* cblk, int64_t coff, float* stage_w)
+                                                   int nsteps, uint32_t t_row, int col0, const OutRows& o,
+                                                   float* stage_w)
 {
+    staging_free(p);
     const int lane = threadIdx.x & 31;
     const int half = warp >> 2;
     const int row = (warp & 3) * 32 + lane;
@@ -928,7 +977,7 @@ __device__ __forceinline__ bool softmax_bwd_tile_ring(const GemmParams& p, const
             tmem_ld32(t_row + c, r);
 #pragma unroll
             for (int j = 0; j < 32; ++j) pr[j] = pr[j] * (p.alpha * __uint_as_float(r[j]) - sum);
-            store_block_out(p, pm, stage_w, pr, cblk, brows, coff, wrow0, c, min(32, p.N - c));
+            store_block_out(p, pm, stage_w, pr, o, c, min(32, p.N - c));
         }
     }
     return true;
@@ -950,6 +999,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ CUtensorMap tmAlo,
                       const __grid_constant__ CUtensorMap tmBlo,
                       const __grid_constant__ CUtensorMap tmP,
+                      const __grid_constant__ CUtensorMap tmC,
                       const __grid_constant__ GemmParams p,
                       const __grid_constant__ PeerMaps pm)
 {
@@ -1006,6 +1056,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     }
     if (kRow == kRowSoftmaxBwd && p.p_tma && warp == kExportWarp0 && lane == 0) tma_prefetch_map(&tmP);
+    if (p.c_tma && threadIdx.x == 0) tma_prefetch_map(&tmC);
     if (warp == kMmaWarp) {
         if (kPair) {
             tmem_alloc_pair(smem_u32(&ss->tmem_base), L::kTmemCols);
@@ -1045,6 +1096,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int n0 = tc.nt * BN + (int)rank * L::kBRows;
                 int red_step = -1;
                 for (int kb = u.kb0; kb < u.kb1; ++kb) {
+                    if (p.test_stall && ui == 0 && kb > u.kb0) {
+                        // failure-path test: this stage is never loaded, so the
+                        // roles waiting for it run out their (shortened) limit
+                        ok = false;
+                        break;
+                    }
                     if (!wait_phase<0>(smem_u32(&ss->empty[stage]), phase ^ 1u, ss, p, kWaitProducerEmpty)) {
                         ok = false;
                         break;
@@ -1458,7 +1515,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             // of its rows are inside the matrix
             const int wrow0 = m0 + sub * 32;
             const int brows = max(0, min(32, p.M - wrow0));
-            float* cblk = p.C + coff + (int64_t)(brows > 0 ? wrow0 + (p.export_peers ? p.peer_row0 : 0) : 0) * p.ldc;
+            OutRows orow;
+            orow.blk = p.C + coff + (int64_t)(brows > 0 ? wrow0 + (p.export_peers ? p.peer_row0 : 0) : 0) * p.ldc;
+            orow.rows = brows;
+            orow.row0 = wrow0;
+            orow.coff = coff;
+            orow.map = &tmC;
+            orow.cc[0] = orow.cc[1] = orow.cc[2] = 0;
+            if (p.c_tma) batch_coords(p, idx, p.c_map, p.c_mult, orow.cc);
             // export mode: this GPU's full C, at this rank's row offset
             const int64_t crow_idx = rok ? gm + (p.export_peers ? p.peer_row0 : 0) : 0;
             float* crow = p.C + coff + crow_idx * p.ldc;
@@ -1468,8 +1532,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             if constexpr (softmax) {
                 // row softmax (N <= BN, one n-tile): softmax_tile
-                if (!softmax_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, wrow0, gm,
-                                  has_bias && rok ? brow : nullptr, cblk, brows, coff, stage_w)) {
+                if (!softmax_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, gm,
+                                  has_bias && rok ? brow : nullptr, orow, stage_w)) {
                     ok = false;
                     break;
                 }
@@ -1477,9 +1541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // fused softmax backward (N <= BN, one n-tile): softmax_bwd_tile
                 const bool done = p.p_tma
                     ? softmax_bwd_tile_ring(p, pm, ss, warp, meet_seq, p_slot, p_phase, L::kHalfChunks, t_row,
-                                            c_lo * 32, wrow0, brows, cblk, coff, stage_w)
-                    : softmax_bwd_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, wrow0, cblk, coff,
-                                       stage_w);
+                                            c_lo * 32, orow, stage_w)
+                    : softmax_bwd_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, orow, stage_w);
                 if (!done) {
                     ok = false;
                     break;
@@ -1504,7 +1567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j)
                             if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
                     }
-                    store_block_out(p, pm, stage_w, v, cblk, brows, coff, wrow0, gn0, nvalid);
+                    store_block_out(p, pm, stage_w, v, orow, gn0, nvalid);
                 }
             }
             tc_fence_before();
@@ -1525,6 +1588,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) atomicAdd(&ss->tiles_stored, 1u);
             }
+        }
+        // this CTA's TMA stores of C have completed before it exits
+        if (p.c_tma) {
+            if (lane == 0) bulk_wait_all();
+            __syncwarp();
         }
         // remote rows (fused all-gather) have landed and are visible
         // system-wide before the kernel is seen as complete

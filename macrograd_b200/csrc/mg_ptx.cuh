@@ -125,6 +125,36 @@ __device__ __forceinline__ void tma_load(const CUtensorMap* map, uint32_t bar, u
 }
 
 // Tiled tensor store of one box from shared memory (bulk-group completion).
+// Tiled tensor store of one box from this CTA's shared memory (bulk group
+// completion; rank 2..5, coordinates innermost first).
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, uint32_t src, int rank, int32_t c0, int32_t c1,
+                                          int32_t c2, int32_t c3, int32_t c4)
+{
+    const uint64_t m = reinterpret_cast<uint64_t>(map);
+    switch (rank) {
+    case 2:
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(m), "r"(src),
+                     "r"(c0), "r"(c1)
+                     : "memory");
+        break;
+    case 3:
+        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(m),
+                     "r"(src), "r"(c0), "r"(c1), "r"(c2)
+                     : "memory");
+        break;
+    case 4:
+        asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(m),
+                     "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                     : "memory");
+        break;
+    default:
+        asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(m),
+                     "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+                     : "memory");
+        break;
+    }
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t c0, int32_t c1)
 {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(

@@ -5,6 +5,7 @@
 // Used by the drop-in tests: the reference's own Functional::matmul and its
 // autograd backward, called exactly as a Macrograd user would, must reach the
 // sm_100a kernels and agree with the oracle.
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <vector>
@@ -74,6 +75,41 @@ int seam_matmul_backward(float* dA, float* dB, float* dbias, const float* A, con
     to_host(b.gradient(), dB);
     if (bias && dbias) to_host(bi.gradient(), dbias);
     return 0;
+}
+
+// A used by two products: loss = sum(A W1 * dC1) + sum(A W2 * dC2), so the
+// reference autograd accumulates A's gradient twice -- the second time into a
+// gradient that already holds the first product's share.
+int seam_shared_operand_backward(float* dA, const float* A, const float* W1, const float* W2, const float* dC1,
+                                 const float* dC2, const int32_t* A_shape, const int32_t* W_shape,
+                                 const int32_t* C_shape, int32_t rank)
+{
+    Tensor a = to_cuda(A, A_shape, rank, true);
+    Tensor w1 = to_cuda(W1, W_shape, rank, false);
+    Tensor w2 = to_cuda(W2, W_shape, rank, false);
+    Tensor g1 = to_cuda(dC1, C_shape, rank, false);
+    Tensor g2 = to_cuda(dC2, C_shape, rank, false);
+    Tensor loss = (Functional::matmul(a, w1) * g1).flatten().sum(0) + (Functional::matmul(a, w2) * g2).flatten().sum(0);
+    loss.backward();
+    to_host(a.gradient(), dA);
+    return 0;
+}
+
+// Milliseconds per Functional::matmul of two n x n "cuda" tensors through the
+// reference's API (output allocation included), over `iters` calls after
+// `warmup`, host-timed around a device synchronisation.
+double seam_time_matmul(int32_t n, int32_t warmup, int32_t iters)
+{
+    const int32_t s[2] = {n, n};
+    Tensor a(make_shape(s, 2), "cuda", false);
+    Tensor b(make_shape(s, 2), "cuda", false);
+    for (int32_t i = 0; i < warmup; ++i) Tensor c = Functional::matmul(a, b);
+    Cuda::synchronize();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (int32_t i = 0; i < iters; ++i) Tensor c = Functional::matmul(a, b);
+    Cuda::synchronize();
+    const auto t1 = std::chrono::steady_clock::now();
+    return std::chrono::duration<double, std::milli>(t1 - t0).count() / (iters > 0 ? iters : 1);
 }
 
 void seam_synchronize(void) { Cuda::synchronize(); }
