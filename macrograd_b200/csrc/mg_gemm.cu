@@ -1087,6 +1087,12 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.alpha = d->alpha;
     gp.beta = d->beta;
     gp.epi = d->epilogue;
+    // causal row softmax: a tile's work grows with its m-tile (the live
+    // columns end at the diagonal), and consecutive tiles alternate m-tiles of
+    // the same batch; mirrored waves give each CTA both kinds in turn instead
+    // of one kind every wave (an even CTA count keeps a tile's parity)
+    gp.plan.mirror = ((d->epilogue & mg::kEpiSoftmax) && (d->epilogue & mg::kEpiCausal) &&
+                      tuning_int("MG_GEMM_MIRROR", 1, 0, 1)) ? 1 : 0;
     gp.status = dev->status;
     // bounded waits: 4 s, unless shortened (MG_GEMM_WAIT_LIMIT_MS, 1..4000);
     // MG_GEMM_TEST_STALL=1 withholds every CTA's second K-block so that a test

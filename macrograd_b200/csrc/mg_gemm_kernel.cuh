@@ -264,6 +264,19 @@ __device__ __forceinline__ void batch_index(int b, const GemmParams& p, int* idx
 constexpr int kSharedStateBytes = 1024;  // SharedState, padded; the epilogue staging blocks follow
                                          // (1024-byte aligned: TMA stores read them 128B-swizzled)
 
+// What the epilogue warps need of one work unit, worked out ahead of time by
+// the producer thread (tile decoding and batch offsets take divisions and
+// parameter loads: hundreds of cycles of one warp's latency per tile, which
+// the epilogue would otherwise spend between tiles). kind -1: no more units.
+struct UnitRec {
+    int kind, slot, nsib;   // Unit::kind, slot, nsib
+    int n_chunks;           // promotion chunks of the unit's K-range
+    int tile, mt, nt;
+    int cc[3];              // C tensor map batch coordinates (p.c_tma)
+    int64_t coff, boff;     // C and bias batch offsets (elements)
+};
+constexpr int kRecSlots = 4;
+
 struct SharedState {
     uint64_t full[kMaxStages];        // local: TMA landed
     uint64_t split_done[kMaxStages];  // MMA issuer's CTA: stage ready in every CTA
@@ -279,6 +292,9 @@ struct SharedState {
     uint64_t pair_bar[kEpiWarps / 2]; // row epilogues: epilogue warps w and w ^ 4 met (64 arrivals)
     uint64_t p_full[kPRingSlots];     // softmax backward: a step of P landed in the ring slot
     uint64_t p_empty[kPRingSlots];    // ... every epilogue warp is done with the slot
+    uint64_t rec_full[kRecSlots];     // the producer wrote unit record `rec` of the slot
+    uint64_t rec_empty[kRecSlots];    // ... every epilogue warp has read it
+    UnitRec rec[kRecSlots];
 };
 
 static_assert(sizeof(SharedState) <= kSharedStateBytes, "SharedState outgrew its slot");
@@ -329,6 +345,61 @@ __device__ __forceinline__ void drain_phase(uint32_t bar, uint32_t parity)
     while (!mbar_test(bar, parity)) {
         if (global_timer_ns() - t0 > kDrainLimitNs) return;
     }
+}
+
+// Producer side of the unit records: waits until the epilogue warps have read
+// the slot's previous record, writes unit ui's (u null: the end marker) and
+// marks it written (the arrive releases the writes). Single thread.
+__device__ __forceinline__ bool post_unit_rec(SharedState* ss, const GemmParams& p, int ui, const Unit* u,
+                                              const TileCoord& tc, const int* idx)
+{
+    const int rs = ui % kRecSlots;
+    if (!wait_phase<0>(smem_u32(&ss->rec_empty[rs]), ((uint32_t)(ui / kRecSlots) & 1u) ^ 1u, ss, p,
+                       kWaitProducerEmpty))
+        return false;
+    UnitRec& r = ss->rec[rs];
+    if (u == nullptr) {
+        r.kind = -1;
+    } else {
+        r.kind = u->kind;
+        r.slot = u->slot;
+        r.nsib = u->nsib;
+        r.n_chunks = (u->kb1 - u->kb0 + p.chunk_kb - 1) / p.chunk_kb;
+        r.tile = u->tile;
+        r.mt = tc.mt;
+        r.nt = tc.nt;
+        int64_t coff = 0, boff = 0;
+#pragma unroll
+        for (int d = 0; d < kMaxBatchDims; ++d) {
+            if (d < p.nbd) {
+                coff += (int64_t)idx[d] * p.c_bs[d];
+                boff += (int64_t)idx[d] * p.bias_bs[d];
+            }
+        }
+        r.coff = coff;
+        r.boff = boff;
+        int32_t cc[3] = {0, 0, 0};
+        if (p.c_tma) batch_coords(p, idx, p.c_map, p.c_mult, cc);
+        r.cc[0] = cc[0];
+        r.cc[1] = cc[1];
+        r.cc[2] = cc[2];
+    }
+    mbar_arrive(smem_u32(&ss->rec_full[rs]));
+    return true;
+}
+
+// Epilogue side: unit ui's record (bounded wait), then the slot goes back.
+// Warp-collective; false when the wait gave up.
+__device__ __forceinline__ bool take_unit_rec(SharedState* ss, const GemmParams& p, int ui, UnitRec& r)
+{
+    const int rs = ui % kRecSlots;
+    const bool got = wait_phase<1>(smem_u32(&ss->rec_full[rs]), (uint32_t)(ui / kRecSlots) & 1u, ss, p,
+                                   kWaitEpiloguePartial);
+    if (!__all_sync(0xffffffffu, got)) return false;
+    r = ss->rec[rs];
+    __syncwarp();   // every lane holds the record before the slot is handed back
+    if ((threadIdx.x & 31) == 0) mbar_arrive(smem_u32(&ss->rec_empty[rs]));
+    return true;
 }
 
 __host__ __device__ constexpr uint32_t pow2_at_least(uint32_t x, uint32_t p = 32)
@@ -645,12 +716,16 @@ __device__ __forceinline__ float exp2_approx(float x)
 }
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Row softmax passes over one thread's TMEM row, columns [c0, c1) in blocks
-// of 32 (c1 warp-uniform: the TMEM loads are warp-collective). Column n's
-// logit is alpha * acc[n] + brow[n * bcs] (brow null: no bias); columns
-// n >= lim (past N, or past the causal diagonal; per lane) are -inf and their
-// bias is never read. Two 32-column loads share one wait where two blocks
-// remain.
+// Row softmax passes over one thread's TMEM row. The two warps that share a
+// row's TMEM lanes take every other 32-column block of it: this warp the
+// blocks c = c0, c0 + 64, ... below c1 (c0 = 0 or 32; c1 warp-uniform, as
+// the TMEM loads are warp-collective), so under a causal mask both warps
+// keep about the same number of live blocks. Column n's logit is
+// alpha * acc[n] + brow[n * bcs] (brow null: no bias); columns n >= lim
+// (past N, or past the causal diagonal; per lane) are -inf and their bias is
+// never read. Blocks that end at or before `full` (warp-uniform: no lane of
+// the warp masks them) skip the per-column test. Max, sum: four interleaved
+// partial results per block, so no pass is one long dependency chain.
 __device__ __forceinline__ float logit_of(uint32_t acc, int n, int lim, float alpha, const float* brow, int64_t bcs)
 {
     if (n >= lim) return -INFINITY;
@@ -659,91 +734,98 @@ __device__ __forceinline__ float logit_of(uint32_t acc, int n, int lim, float al
     return x;
 }
 
-// Max of the live logits. Without a bias it is taken on the raw
-// accumulators: rounding is monotone, so max_n fl(alpha acc[n]) =
-// fl(|alpha| max_n (sign(alpha) acc[n])) exactly. `biased` must be
-// warp-uniform (some lanes of a biased warp may have no bias row): the TMEM
-// loads inside its two branches are warp-collective.
-__device__ __forceinline__ float softmax_row_max(uint32_t t_row, int c0, int c1, int lim, float alpha,
-                                                 const float* brow, int64_t bcs, bool biased)
+__device__ __forceinline__ void block_max(const uint32_t (&r)[32], int c, int lim, int full, float (&m)[4])
 {
-    float mx = -INFINITY;
-    int c = c0;
-    if (!biased) {
-        const uint32_t sign = alpha < 0.f ? 0x80000000u : 0u;
-        for (; c + 32 < c1; c += 64) {
+    if (c + 32 <= full) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m[j & 3] = fmaxf(m[j & 3], __uint_as_float(r[j]));
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) m[j & 3] = fmaxf(m[j & 3], c + j < lim ? __uint_as_float(r[j]) : -INFINITY);
+    }
+}
+
+// Max of the live logits. `plain` (no bias, alpha >= 0; warp-uniform) takes
+// it on the raw accumulators: rounding is monotone, so
+// max_n fl(alpha acc[n]) = fl(alpha max_n acc[n]) exactly. Otherwise each
+// column's logit is formed first (some lanes of a biased warp may have no
+// bias row).
+__device__ __forceinline__ float softmax_row_max(uint32_t t_row, int c0, int c1, int lim, int full, float alpha,
+                                                 const float* brow, int64_t bcs, bool plain)
+{
+    float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (plain) {
+        int c = c0;
+        for (; c + 64 < c1; c += 128) {
             uint32_t r[32], q[32];
-            tmem_ld32x2(t_row + c, r, t_row + c + 32, q);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, c + j < lim ? __uint_as_float(r[j] ^ sign) : -INFINITY);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, c + 32 + j < lim ? __uint_as_float(q[j] ^ sign) : -INFINITY);
+            tmem_ld32x2(t_row + c, r, t_row + c + 64, q);
+            block_max(r, c, lim, full, m);
+            block_max(q, c + 64, lim, full, m);
         }
         if (c < c1) {
             uint32_t r[32];
             tmem_ld32(t_row + c, r);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) mx = fmaxf(mx, c + j < lim ? __uint_as_float(r[j] ^ sign) : -INFINITY);
+            block_max(r, c, lim, full, m);
         }
-        return mx == -INFINITY ? mx : fabsf(alpha) * mx;
+        const float mx = fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+        return mx == -INFINITY ? mx : alpha * mx;
     }
-    for (; c + 32 < c1; c += 64) {
-        uint32_t r[32], q[32];
-        tmem_ld32x2(t_row + c, r, t_row + c + 32, q);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, logit_of(r[j], c + j, lim, alpha, brow, bcs));
-#pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, logit_of(q[j], c + 32 + j, lim, alpha, brow, bcs));
-    }
-    if (c < c1) {
+    for (int c = c0; c < c1; c += 64) {
         uint32_t r[32];
         tmem_ld32(t_row + c, r);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, logit_of(r[j], c + j, lim, alpha, brow, bcs));
+        for (int j = 0; j < 32; ++j) m[j & 3] = fmaxf(m[j & 3], logit_of(r[j], c + j, lim, alpha, brow, bcs));
     }
-    return mx;
+    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
 }
 
-// exp(logit - mx) of one 32-column block, in place (0 for the -inf columns);
-// returns `sum` plus the block's values, added in column order.
-__device__ __forceinline__ float exp_block(uint32_t (&r)[32], int c, int lim, float alpha, const float* brow,
-                                           int64_t bcs, bool biased, float mx2, float sum)
+// exp(logit - mx) of one 32-column block, in place (0 for the -inf
+// columns), added into the four partial sums.
+__device__ __forceinline__ void exp_block(uint32_t (&r)[32], int c, int lim, int full, float alpha, const float* brow,
+                                          int64_t bcs, bool plain, float mx2, float (&s)[4])
 {
-    if (!biased) {
+    if (plain) {
         const float a2 = alpha * kLog2e;
+        if (c + 32 <= full) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            const float e = c + j < lim ? exp2_approx(fmaf(__uint_as_float(r[j]), a2, -mx2)) : 0.f;
-            sum += e;
-            r[j] = __float_as_uint(e);
+            for (int j = 0; j < 32; ++j) {
+                const float e = exp2_approx(fmaf(__uint_as_float(r[j]), a2, -mx2));
+                s[j & 3] += e;
+                r[j] = __float_as_uint(e);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float e = c + j < lim ? exp2_approx(fmaf(__uint_as_float(r[j]), a2, -mx2)) : 0.f;
+                s[j & 3] += e;
+                r[j] = __float_as_uint(e);
+            }
         }
-        return sum;
+        return;
     }
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const float x = logit_of(r[j], c + j, lim, alpha, brow, bcs);
         const float e = x != -INFINITY ? exp2_approx(fmaf(x, kLog2e, -mx2)) : 0.f;
-        sum += e;
+        s[j & 3] += e;
         r[j] = __float_as_uint(e);
     }
-    return sum;
 }
 
-// exp(logit - mx) back into the row's columns [c0, c1); returns their sum,
-// accumulated in column order.
-__device__ __forceinline__ float softmax_row_exp(uint32_t t_row, int c0, int c1, int lim, float alpha,
-                                                 const float* brow, int64_t bcs, bool biased, float mx)
+// exp(logit - mx) back into this warp's blocks of the row; returns their sum.
+__device__ __forceinline__ float softmax_row_exp(uint32_t t_row, int c0, int c1, int lim, int full, float alpha,
+                                                 const float* brow, int64_t bcs, bool plain, float mx)
 {
     const float mx2 = mx * kLog2e;
-    float sum = 0.f;
-    for (int c = c0; c < c1; c += 32) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = c0; c < c1; c += 64) {
         uint32_t r[32];
         tmem_ld32(t_row + c, r);
-        sum = exp_block(r, c, lim, alpha, brow, bcs, biased, mx2, sum);
+        exp_block(r, c, lim, full, alpha, brow, bcs, plain, mx2, s);
         tmem_st32_async(t_row + c, r);
     }
     tmem_wait_st();   // the exps are in TMEM before the scaling pass reads them
-    return sum;
+    return (s[0] + s[1]) + (s[2] + s[3]);
 }
 
 // This lane's row of a 32 x 32 block of P (rows blk_row0 .., columns c ..):
@@ -827,19 +909,20 @@ __device__ __forceinline__ void softmax_bwd_out(const GemmParams& p, const PeerM
     }
 }
 
-// The row softmax epilogue of one tile, for the thread's row gm and its
-// column half [col0, col1) (TMEM row t_row; the warp's rows start at wrow0).
-// A row lives in one TMEM lane; warp w and its partner w ^ 4 hold its two
-// column halves. Each thread takes its half's max, the pair meets (pair_meet:
-// posts in the warps' staging blocks), exp(x - max) goes back into the row's
-// TMEM columns while summing, the pair meets for the sum (and once more before
-// the staging block is reused), then the scaled values leave. Semantics of
-// Tensor::softmax (tensor_ops.cpp:2093-2112): max, expf, sum in column order
-// (first half, then second), divide (here: multiply by the rounded
-// reciprocal). Returns false when a meeting gave up (abort). Out of line: one
-// call per tile keeps the main epilogue loop's registers free.
+// The row softmax epilogue of one tile, for the thread's row gm (TMEM row
+// t_row; the warp's rows start at o.row0). A row lives in one TMEM lane; warp
+// w and its partner w ^ 4 hold its 32-column blocks alternately (warp w the
+// blocks from col0 = 32 * (w >> 2) on, every 64 columns). Each thread takes
+// the max over its blocks, the pair meets (pair_meet: posts in the warps'
+// staging blocks), exp(x - max) goes back into the blocks' TMEM columns while
+// summing, the pair meets for the sum (and once more before the staging block
+// is reused), then the scaled values leave. Semantics of Tensor::softmax
+// (tensor_ops.cpp:2093-2112): max, expf, sum, divide (here: multiply by the
+// rounded reciprocal); the sum is formed as eight partial sums (four per
+// warp), so its rounding differs from the reference's single running sum by
+// a few ulp. Returns false when a meeting gave up (abort).
 __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps& pm, SharedState* ss, int warp,
-                                          unsigned int& meet_seq, uint32_t t_row, int col0, int col1, int gm,
+                                          unsigned int& meet_seq, uint32_t t_row, int col0, int gm,
                                           const float* bias_row, const OutRows& o, float* stage_w)
 {
     const int wrow0 = o.row0;
@@ -849,29 +932,30 @@ __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps
     const bool causal = (p.epi & kEpiCausal) != 0;
     float* xch = stage_w;                                                    // my posts
     const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;   // partner's
-    // live columns: [0, N), and up to the diagonal when causal; wlim bounds
-    // every lane of the warp (rows wrow0 .. + 31), so the chunk loops -- and
-    // their warp-collective TMEM loads -- stay warp-uniform
+    // live columns: [0, N), and up to the diagonal when causal. wlim bounds
+    // every lane of the warp (rows wrow0 .. + 31), so the block loops -- and
+    // their warp-collective TMEM loads -- stay warp-uniform; below `full` no
+    // lane masks a column
     const int lim = causal ? min(p.N, gm + 1) : p.N;
     const int wlim = causal ? min(p.N, wrow0 + 32) : p.N;
-    const int c1 = min(col1, wlim);
+    const int full = causal ? min(p.N, wrow0 + 1) : p.N;
     // the bias path for the whole warp when any of its rows has a bias row
     // (rows past M have none): a warp-uniform choice of code with collective loads
-    const bool biased = __any_sync(0xffffffffu, bias_row != nullptr);
-    float mx = softmax_row_max(t_row, col0, c1, lim, p.alpha, bias_row, p.bias_cs, biased);
+    const bool plain = !__any_sync(0xffffffffu, bias_row != nullptr) && p.alpha >= 0.f;
+    float mx = softmax_row_max(t_row, col0, wlim, lim, full, p.alpha, bias_row, p.bias_cs, plain);
     xch[lane] = mx;
     if (!pair_meet(ss, warp, meet_seq, p)) return false;
     mx = fmaxf(mx, pxch[lane]);
-    float sum = softmax_row_exp(t_row, col0, c1, lim, p.alpha, bias_row, p.bias_cs, biased, mx);
+    float sum = softmax_row_exp(t_row, col0, wlim, lim, full, p.alpha, bias_row, p.bias_cs, plain, mx);
     xch[32 + lane] = sum;
     if (!pair_meet(ss, warp, meet_seq, p)) return false;
-    // the row's sum: first half's columns, then the second half's
+    // the row's sum, added in the same order by both warps
     sum = half ? pxch[32 + lane] + sum : sum + pxch[32 + lane];
     // the partner has read this block before the stores reuse it
     if (!pair_meet(ss, warp, meet_seq, p)) return false;
     const float inv = 1.f / sum;
     const float dead = 0.f * inv;   // columns no lane of the warp reaches (NaN if the whole row is)
-    for (int c = col0; c < col1 && c < p.N; c += 32) {
+    for (int c = col0; c < p.N; c += 64) {
         float v[32];
         if (c < wlim) {
             uint32_t r[32];
@@ -1045,6 +1129,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(smem_u32(&ss->p_full[q]), 1);
             mbar_init(smem_u32(&ss->p_empty[q]), kEpiWarps);
         }
+        for (int q = 0; q < kRecSlots; ++q) {
+            mbar_init(smem_u32(&ss->rec_full[q]), 1);
+            mbar_init(smem_u32(&ss->rec_empty[q]), kEpiWarps);
+        }
         mbar_fence_init();
     }
     if (warp == kProducerWarp && lane == 0) {
@@ -1084,10 +1172,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t issued = 0, issued_par = 0;
             bool ok = true;
             Unit u;
-            for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
+            int ui = 0;
+            for (; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
                 const TileCoord tc = decode_tile(u.tile, p);
                 int idx[kMaxBatchDims];
                 batch_index(tc.batch, p, idx);
+                if (!post_unit_rec(ss, p, ui, &u, tc, idx)) {
+                    ok = false;
+                    break;
+                }
                 int32_t ta[3] = {0, 0, 0}, tb[3] = {0, 0, 0};   // the tile's batch coordinates
                 batch_coords(p, idx, p.a_map, p.a_mult, ta);
                 batch_coords(p, idx, p.b_map, p.b_mult, tb);
@@ -1151,6 +1244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (++stage == stages) { stage = 0; phase ^= 1u; }
                 }
             }
+            if (ok) ok = post_unit_rec(ss, p, ui, nullptr, TileCoord{}, nullptr);   // no more units
             if (!ok) {
                 // let every issued copy land before the CTA's shared memory goes away
                 for (int s = 0; s < stages; ++s)
@@ -1420,10 +1514,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         int p_slot = 0;              // softmax backward with the P ring: the next slot and its phase
         uint32_t p_phase = 0;
         bool ok = true;
-        Unit u;
-        for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
-            const TileCoord tc = decode_tile(u.tile, p);
-            const int n_chunks = (u.kb1 - u.kb0 + p.chunk_kb - 1) / p.chunk_kb;
+        for (int ui = 0; ok; ++ui) {
+            UnitRec u;   // the unit, decoded by the producer
+            if (!take_unit_rec(ss, p, ui, u)) {
+                ok = false;
+                break;
+            }
+            if (u.kind < 0) break;
+            const int n_chunks = u.n_chunks;
             const int rg = p.dbuf ? (ui & 1) : 0;
             if (p.dbuf) {
                 // one chunk: the accumulator itself is the result
@@ -1496,18 +1594,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 
             // ---- output epilogue from the master
-            int idx[kMaxBatchDims];
-            batch_index(tc.batch, p, idx);
-            int64_t coff = 0, boff = 0;
-#pragma unroll
-            for (int d = 0; d < kMaxBatchDims; ++d) {
-                if (d < p.nbd) {
-                    coff += (int64_t)idx[d] * p.c_bs[d];
-                    boff += (int64_t)idx[d] * p.bias_bs[d];
-                }
-            }
-            const int m0 = tc.mt * L::kTileRows + (int)rank * kBM;
-            const int n0 = tc.nt * BN;
+            const int64_t coff = u.coff, boff = u.boff;
+            const int m0 = u.mt * L::kTileRows + (int)rank * kBM;
+            const int n0 = u.nt * BN;
             const int gm = m0 + row;
             const bool rok = gm < p.M;
             // this warp's 32-row output block: its first row in C (export
@@ -1521,8 +1610,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             orow.row0 = wrow0;
             orow.coff = coff;
             orow.map = &tmC;
-            orow.cc[0] = orow.cc[1] = orow.cc[2] = 0;
-            if (p.c_tma) batch_coords(p, idx, p.c_map, p.c_mult, orow.cc);
+            orow.cc[0] = u.cc[0];
+            orow.cc[1] = u.cc[1];
+            orow.cc[2] = u.cc[2];
             // export mode: this GPU's full C, at this rank's row offset
             const int64_t crow_idx = rok ? gm + (p.export_peers ? p.peer_row0 : 0) : 0;
             float* crow = p.C + coff + crow_idx * p.ldc;
@@ -1532,8 +1622,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
             if constexpr (softmax) {
                 // row softmax (N <= BN, one n-tile): softmax_tile
-                if (!softmax_tile(p, pm, ss, warp, meet_seq, t_row, c_lo * 32, c_hi * 32, gm,
-                                  has_bias && rok ? brow : nullptr, orow, stage_w)) {
+                if (!softmax_tile(p, pm, ss, warp, meet_seq, t_row, 32 * half, gm, has_bias && rok ? brow : nullptr,
+                                  orow, stage_w)) {
                     ok = false;
                     break;
                 }

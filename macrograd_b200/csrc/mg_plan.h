@@ -27,6 +27,7 @@ constexpr int kMaxLevels = 4;
 
 struct UnitPlan {
     int full_tiles;     // whole tiles [0, full_tiles), round-robin
+    int mirror;         // odd waves dealt in reverse unit order (unit u takes position U - 1 - u)
     int nlev;           // split levels after them
     int num_kb;         // K-blocks of a whole tile
     int lev_split[kMaxLevels], lev_tiles[kMaxLevels], lev_tile0[kMaxLevels], lev_slot0[kMaxLevels];
@@ -42,9 +43,14 @@ struct Unit {
 // The i-th unit of unit u0 out of ustep; false past its last one.
 MG_HD bool plan_unit_at(const UnitPlan& w, int u0, int ustep, int i, Unit& u)
 {
-    const int nw = w.full_tiles > u0 ? (w.full_tiles - u0 + ustep - 1) / ustep : 0;
+    // whole tiles: wave v holds tiles [v * ustep, (v + 1) * ustep); the unit's
+    // position in wave v is u0, or ustep - 1 - u0 on odd waves when mirrored
+    // (a unit then alternates between even and odd tile positions)
+    const int waves = w.full_tiles / ustep, rem = w.full_tiles - waves * ustep;
+    const int last_pos = (w.mirror && (waves & 1)) ? ustep - 1 - u0 : u0;
+    const int nw = waves + (last_pos < rem ? 1 : 0);
     if (i < nw) {
-        u.tile = u0 + i * ustep;
+        u.tile = i * ustep + ((w.mirror && (i & 1)) ? ustep - 1 - u0 : u0);
         u.kb0 = 0;
         u.kb1 = w.num_kb;
         u.kind = 0;

@@ -18,10 +18,13 @@ static int fail(const char* what, int T, int U, int KB, int mk)
 
 // Every (tile, K-block) is covered exactly once; partial slots are written by
 // exactly one range of their tile and read by that tile's final range; a
-// split never makes any unit's work longer than whole-tile waves would.
-static int check(int T, int U, int KB, int mk, int* nsplit)
+// split never makes any unit's work longer than whole-tile waves would. With
+// `mirror` the whole-tile waves alternate direction: a unit's tiles then
+// alternate between even and odd positions (when the unit count is even).
+static int check(int T, int U, int KB, int mk, int* nsplit, int mirror = 0)
 {
-    UnitPlan w;
+    UnitPlan w{};
+    w.mirror = mirror;
     const int nslots = mg::plan_k_split(w, T, U, KB, mk);
     if (w.nlev > 0) ++*nsplit;
     if ((nslots > 0) != (w.nlev > 0)) return fail("slot count vs levels", T, U, KB, mk);
@@ -32,8 +35,11 @@ static int check(int T, int U, int KB, int mk, int* nsplit)
     int worst = 0;
     for (int u0 = 0; u0 < grid; ++u0) {
         Unit u;
-        int work = 0;
+        int work = 0, prev_whole = -1;
         for (int i = 0; mg::plan_unit_at(w, u0, grid, i, u); ++i) {
+            if (mirror && u.kind == 0 && grid % 2 == 0 && prev_whole >= 0 && (u.tile - prev_whole) % 2 == 0)
+                return fail("mirrored waves: consecutive whole tiles of a unit share a parity", T, U, KB, mk);
+            if (u.kind == 0) prev_whole = u.tile;
             if (u.tile < 0 || u.tile >= T || u.kb0 < 0 || u.kb1 > KB || u.kb0 >= u.kb1)
                 return fail("unit out of range", T, U, KB, mk);
             for (int kb = u.kb0; kb < u.kb1; ++kb) cover[(size_t)u.tile * KB + kb]++;
@@ -69,7 +75,7 @@ static int check(int T, int U, int KB, int mk, int* nsplit)
 
 static int expect(int T, int U, int KB, int mk, int nlev, const int* split, const int* tiles)
 {
-    UnitPlan w;
+    UnitPlan w{};
     mg::plan_k_split(w, T, U, KB, mk);
     if (w.nlev != nlev) return fail("unexpected level count", T, U, KB, mk);
     for (int l = 0; l < nlev; ++l)
@@ -125,10 +131,10 @@ int main()
         for (int U : units)
             for (int KB : kbs)
                 for (int mk : mks)
-                    if (check(T, U, KB, mk, &nsplit)) return 1;
+                    if (check(T, U, KB, mk, &nsplit) || check(T, U, KB, mk, &nsplit, 1)) return 1;
     for (int T : {512, 1024, 1184, 2048})
         for (int U : units)
-            if (check(T, U, 256, 16, &nsplit)) return 1;
+            if (check(T, U, 256, 16, &nsplit) || check(T, U, 256, 16, &nsplit, 1)) return 1;
     // the row-sharded 8192^3 shapes on 74 SM pairs
     const int s8[] = {2, 4}, t8[] = {37, 17};
     const int s4[] = {2}, t4[] = {34};

@@ -241,6 +241,29 @@ def test_kernel_variants_softmax_and_accumulate(kernel_variant):
     assert_close(host(g), prev + dW, 0, f"beta=1 {kernel_variant}")
 
 
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("M,N", [(40, 17), (64, 64), (100, 100), (70, 130), (256, 256), (300, 250)])
+@pytest.mark.parametrize("scale", [0.125, -0.5])
+def test_row_softmax_widths_and_scales(mode, M, N, scale):
+    """The fused row softmax at every tile width it runs at (N up to 64, 128
+    and 256 columns, ragged ends, M != N), its two warps' alternating 32-column
+    blocks, causal and not, a negative scale (the per-column path) and an
+    additive mask (the bias path), against the oracle."""
+    set_mode(mode)
+    q = ob.seeded_normal((2, 3, M, 40), 871 + M, 0.0, 0.5)
+    k = ob.seeded_normal((2, 3, N, 40), 872 + N, 0.0, 0.5)
+    add = ob.seeded_normal((M, N), 873 + M + N)
+    causal_mask = np.where(np.arange(N)[None, :] > np.arange(M)[:, None], -np.inf, 0.0).astype(np.float32)
+    for what, causal, mask in (("causal", True, None), ("full", False, None), ("mask", False, add)):
+        P = host(F.attention_scores(cuda(q), cuda(k), scale, causal=causal,
+                                    mask=cuda(mask) if mask is not None else None))
+        ref_mask = causal_mask if causal else mask
+        for b in range(2):
+            for h in range(3):
+                S = ob.oracle_matmul(q[b, h] * np.float32(scale), k[b, h], False, True, ref_mask)
+                assert_close(P[b, h], ob.oracle_softmax_rows(S), mode, f"{what} softmax {M}x{N} scale {scale}")
+
+
 @pytest.mark.parametrize("pair", ["1", "0"], ids=["sm_pair", "single_sm"])
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("sa,sb,ta,tb,bias_shape", [
