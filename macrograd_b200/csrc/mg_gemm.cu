@@ -619,6 +619,21 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     int stages = (int)((size_t)(dev->max_smem - (int)fixed) / per_stage);
     stages = std::min(stages, mg::kMaxStages);
     if (stages < 2) return fail(MG_ERR_UNSUPPORTED, "not enough shared memory for a 2-stage pipeline");
+    // A second staging block per epilogue warp (two TMA stores of C in flight
+    // a warp) where it costs no operand stage the K loop can use: stages to
+    // spare, or short K (every K-block of a tile resident at once).
+    // MG_GEMM_STAGE_BLOCKS=1 / 2 forces one / two where two stages still fit.
+    gp.stage_blocks = 1;
+    if (kRow != mg::kRowSoftmaxBwd && gp.c_tma) {
+        const size_t more = (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4;
+        const int stages2 = std::min((int)((size_t)(dev->max_smem - (int)(fixed + more)) / per_stage), mg::kMaxStages);
+        const int want = tuning_int("MG_GEMM_STAGE_BLOCKS", 0, 0, 2);
+        if (stages2 >= 2 && (want == 2 || (want == 0 && stages2 >= std::min(stages, gp.num_kb)))) {
+            gp.stage_blocks = 2;
+            fixed += more;
+            stages = stages2;
+        }
+    }
     gp.stages = stages;
     const size_t smem = fixed + per_stage * stages;
     auto k = kernel_of<BN, kPair, kRow>();

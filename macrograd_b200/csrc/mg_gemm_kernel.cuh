@@ -148,6 +148,8 @@ struct GemmParams {
     int c_rank;                 // tmC's rank (2 + mapped batch dims)
     int8_t c_map[kMaxBatchDims];
     int32_t c_mult[kMaxBatchDims];
+    int stage_blocks;           // epilogue staging blocks per warp: 2 lets two TMA stores of C
+                                // be in flight per warp (row softmax backward: always 1)
     int p_tma;                  // kEpiSoftmaxBwd: P streamed by TMA (map tmP) into the P ring
     int p_rank;                 // tmP's rank (2 + mapped batch dims)
     int8_t p_map[kMaxBatchDims];
@@ -458,12 +460,46 @@ struct OutRows {
 // Before a warp writes its staging block: with TMA stores, the previous
 // store's read of the block must be over (the write of C itself may still be
 // in flight -- that is the point). Warp-collective.
-__device__ __forceinline__ void staging_free(const GemmParams& p)
+// `pending`: how many of the warp's most recent stores may still be reading
+// their blocks (0 .. 3) -- those that did not read the block about to be
+// written.
+__device__ __forceinline__ void staging_free(const GemmParams& p, int pending = 0)
 {
     if (p.c_tma) {
-        if ((threadIdx.x & 31) == 0) bulk_wait_read_all();
+        if ((threadIdx.x & 31) == 0) {
+            switch (pending) {
+            case 3: bulk_wait_read_n<3>(); break;
+            case 2: bulk_wait_read_n<2>(); break;
+            case 1: bulk_wait_read_n<1>(); break;
+            default: bulk_wait_read_all(); break;
+            }
+        }
         __syncwarp();
     }
+}
+
+// The staging block of this warp's next output store (plain epilogue). With
+// two blocks a warp (p.stage_blocks) they alternate, so a TMA store reads one
+// while the warp fills the other: only the store before last must be done
+// reading (`pending` 1).
+__device__ __forceinline__ float* next_staging(const GemmParams& p, float* stage_w, unsigned int& seq, int& pending)
+{
+    pending = 0;
+    if (p.stage_blocks < 2) return stage_w;
+    float* blk = stage_w + (seq & 1u) * kStageFloatsPerWarp;
+    ++seq;
+    pending = 1;
+    return blk;
+}
+
+// Row epilogues: the warp's k-th store of a tile goes to staging block
+// k % S (S = p.stage_blocks); every tile makes the same number nb of stores.
+// The stores since block k % S was last written -- the previous tile's from
+// the next one of the same block on, this tile's first k -- may still be
+// reading theirs.
+__device__ __forceinline__ int row_store_pending(int k, int nb, int S)
+{
+    return k >= S ? S - 1 : (nb - 1 - k) % S + k;
 }
 
 // Warp-collective store of a 32 x 32 output block (v[j] = column gn0 + j of
@@ -477,10 +513,11 @@ __device__ __forceinline__ void staging_free(const GemmParams& p)
 // row-contiguous by the warp, each store 4 rows x 128 bytes, into C or every
 // rank's C. All 32 lanes must call it.
 __device__ __forceinline__ void store_block_out(const GemmParams& p, const PeerMaps& pm, float* stage,
-                                                const float* v, const OutRows& o, int gn0, int nvalid)
+                                                const float* v, const OutRows& o, int gn0, int nvalid,
+                                                int pending = 0)
 {
     const int lane = threadIdx.x & 31;
-    staging_free(p);
+    staging_free(p, pending);
 #pragma unroll
     for (int q = 0; q < 8; ++q)
         reinterpret_cast<float4*>(stage + lane * 32)[q ^ (lane & 7)] =
@@ -926,12 +963,16 @@ __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps
                                           const float* bias_row, const OutRows& o, float* stage_w)
 {
     const int wrow0 = o.row0;
-    staging_free(p);   // the posts below go into the staging block
     const int lane = threadIdx.x & 31;
     const int half = warp >> 2;
+    // the warp's stores a tile: its blocks below N; the posts below go into
+    // staging block 0, free once the previous tile's store from it has read it
+    const int S = p.stage_blocks;
+    const int nb = (p.N - col0 + 63) / 64;
+    staging_free(p, nb > 0 ? (nb - 1) % S : 0);
     const bool causal = (p.epi & kEpiCausal) != 0;
     float* xch = stage_w;                                                    // my posts
-    const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;   // partner's
+    const float* pxch = stage_w + (half ? -4 : 4) * p.stage_blocks * kStageFloatsPerWarp;   // partner's
     // live columns: [0, N), and up to the diagonal when causal. wlim bounds
     // every lane of the warp (rows wrow0 .. + 31), so the block loops -- and
     // their warp-collective TMEM loads -- stay warp-uniform; below `full` no
@@ -955,7 +996,7 @@ __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps
     if (!pair_meet(ss, warp, meet_seq, p)) return false;
     const float inv = 1.f / sum;
     const float dead = 0.f * inv;   // columns no lane of the warp reaches (NaN if the whole row is)
-    for (int c = col0; c < p.N; c += 64) {
+    for (int k = 0, c = col0; c < p.N; ++k, c += 64) {
         float v[32];
         if (c < wlim) {
             uint32_t r[32];
@@ -966,7 +1007,8 @@ __device__ __forceinline__ bool softmax_tile(const GemmParams& p, const PeerMaps
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = dead;
         }
-        store_block_out(p, pm, stage_w, v, o, c, min(32, p.N - c));
+        store_block_out(p, pm, stage_w + (k % S) * kStageFloatsPerWarp, v, o, c, min(32, p.N - c),
+                        row_store_pending(k, nb, S));
     }
     return true;
 }
@@ -987,7 +1029,7 @@ __device__ __forceinline__ bool softmax_bwd_tile(const GemmParams& p, const Peer
     const int lane = threadIdx.x & 31;
     const int half = warp >> 2;
     float* xch = stage_w;
-    const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;
+    const float* pxch = stage_w + (half ? -4 : 4) * p.stage_blocks * kStageFloatsPerWarp;
     const int wrows = max(0, min(32, p.M - wrow0));     // the warp's rows inside the matrix
     const float* pblk = p.aux + coff + (int64_t)min(wrow0, max(p.M - 1, 0)) * p.ldc;
     const bool pvec = (p.ldc & 3) == 0 && (coff & 3) == 0 && (reinterpret_cast<uintptr_t>(p.aux) & 15u) == 0;
@@ -1017,9 +1059,9 @@ __device__ __forceinline__ bool softmax_bwd_tile_ring(const GemmParams& p, const
     const int half = warp >> 2;
     const int row = (warp & 3) * 32 + lane;
     float* xch = stage_w;
-    const float* pxch = stage_w + (half ? -4 : 4) * kStageFloatsPerWarp;
+    const float* pxch = stage_w + (half ? -4 : 4) * p.stage_blocks * kStageFloatsPerWarp;
     const float* ring = reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(ss) + kSharedStateBytes +
-                                                       (size_t)kEpiWarps * kStageFloatsPerWarp * 4);
+                                                       (size_t)kEpiWarps * p.stage_blocks * kStageFloatsPerWarp * 4);
     // this lane's 32 P values of the slot's box for this half; then the slot goes back
     auto take = [&](float (&pr)[32]) -> bool {
         const bool landed = wait_phase<1>(smem_u32(&ss->p_full[slot]), phase, ss, p, kWaitEpiloguePartial);
@@ -1343,7 +1385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // epilogue warps consume them; plain TMA loads from this GPU's P.
             if (warp == kExportWarp0 && lane == 0) {
                 uint8_t* ring = reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes +
-                                (size_t)kEpiWarps * kStageFloatsPerWarp * 4;
+                                (size_t)kEpiWarps * p.stage_blocks * kStageFloatsPerWarp * 4;
                 int slot = 0;
                 uint32_t phase = 0, issued = 0, issued_par = 0;
                 bool ok = true;
@@ -1505,12 +1547,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t t_part = lane_base;
         const uint32_t t_master = lane_base + (uint32_t)BN;
         float* stage_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes) +
-                         warp * kStageFloatsPerWarp;                  // this warp's store staging block
+                         warp * p.stage_blocks * kStageFloatsPerWarp;   // this warp's store staging block(s)
         const bool has_bias = (p.epi & kEpiBias) != 0;
         constexpr bool softmax = kRow == kRowSoftmax;
         constexpr bool softmax_bwd = kRow == kRowSoftmaxBwd;
         uint32_t chunk_phase = 0;
         unsigned int meet_seq = 0;   // row epilogues: meetings with the partner warp so far
+        unsigned int out_seq = 0;    // output stores so far (alternating staging blocks)
         int p_slot = 0;              // softmax backward with the P ring: the next slot and its phase
         uint32_t p_phase = 0;
         bool ok = true;
@@ -1657,7 +1700,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j)
                             if (j < nvalid) v[j] += p.beta * crow[gn0 + j];
                     }
-                    store_block_out(p, pm, stage_w, v, orow, gn0, nvalid);
+                    int pending;
+                    float* blk = next_staging(p, stage_w, out_seq, pending);
+                    store_block_out(p, pm, blk, v, orow, gn0, nvalid, pending);
                 }
             }
             tc_fence_before();

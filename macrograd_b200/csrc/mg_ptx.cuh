@@ -168,6 +168,10 @@ __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bul
 // The shared-memory sources of this thread's bulk stores have been read.
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
+// All but this thread's N most recent bulk store groups have read their sources.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read_n() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+
 // This thread's bulk stores have completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
