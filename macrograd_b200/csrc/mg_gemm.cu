@@ -759,7 +759,7 @@ bool want_presplit(double flops, int64_t m_tiles, int64_t n_tiles)
 // takes fewer waves over the SM pairs. A K-block costs the pipeline about the
 // same time at either width (its hand-offs, not the MMAs, set the pace), so
 // only the wave count counts and 256 wins ties.
-int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, const DeviceState* dev)
+int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, int64_t red_steps, const DeviceState* dev)
 {
     const int forced = tuning_int("MG_GEMM_BN", 0, 64, 256);
     const bool row_epi = (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) != 0;
@@ -768,9 +768,36 @@ int choose_bn(const mg_gemm_desc* d, bool pair, int64_t nbatch, const DeviceStat
     if (fits && (forced == 64 || forced == 128 || forced == 256 || (forced == 224 && pair && !row_epi)))
         return forced;
     const int base = d->N <= 64 ? 64 : (d->N <= 128 ? 128 : 256);
-    if (!pair || base != 256 || row_epi) return base;
-    const int64_t m_tiles = (d->M + 2 * mg::kBM - 1) / (2 * mg::kBM);
-    const int64_t units = std::max(1, dev->sm_count / 2);
+    if (row_epi) return base;
+    const int64_t m_tiles = (d->M + (pair ? 2 : 1) * mg::kBM - 1) / ((pair ? 2 : 1) * mg::kBM);
+    const int64_t units = std::max(1, pair ? dev->sm_count / 2 : dev->sm_count);
+    // Less than a wave of tiles at the base width: narrower tiles put more
+    // SMs to work, and may make the K split unnecessary. At these sizes a
+    // tile's K loop is paced by its stage hand-offs, not by its width, so the
+    // widths compare by the K-blocks of their busiest unit as the split would
+    // cut them (plan_k_split: up to 8 ranges a tile, ranges of at least 4
+    // K-blocks below half a wave, 16 above), a split's partial-sum exchange
+    // (workspace traffic in proportion to the tile) counted as 3 K-blocks per
+    // 64 columns. Measured: 2048 x 384 x 384 runs 26.6 us at width 64
+    // unsplit, 32.0 us at 256 split three ways; 384 x 384 x (8 x 256) is
+    // faster at 64 split six ways than at 256 split eight ways; the linear
+    // layer's 1536 x 384 x 16384 weight gradient stays at 256 split six ways.
+    auto tiles_at = [&](int bn) { return nbatch * m_tiles * ((d->N + bn - 1) / bn); };
+    if (tiles_at(base) < units) {
+        const int64_t num_kb = std::max<int64_t>(1, (d->K + mg::kBK - 1) / mg::kBK * red_steps);
+        auto busiest = [&](int bn) {
+            const int64_t t = tiles_at(bn);
+            const int64_t min_kb = 2 * t <= units ? 4 : 16;
+            int64_t sp = std::min<int64_t>(std::min<int64_t>(8, units / t), num_kb / min_kb);
+            if (sp < 2) sp = 1;
+            return (num_kb + sp - 1) / sp + (sp > 1 ? 3 * bn / 64 : 0);
+        };
+        int best = base;
+        for (int bn : {128, 64})
+            if (bn < base && tiles_at(bn) <= units && busiest(bn) < busiest(best)) best = bn;
+        return best;
+    }
+    if (!pair || base != 256) return base;
     auto cost = [&](int bn) {
         const int64_t tiles = nbatch * m_tiles * ((d->N + bn - 1) / bn);
         return (tiles + units - 1) / units;   // waves
@@ -974,7 +1001,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     }
 
     const bool pair = use_pair(d, nbatch, dev->sm_count, mode);
-    const int bn = choose_bn(d, pair, nbatch, dev);
+    const int bn = choose_bn(d, pair, nbatch, red_steps, dev);
     const int tile_rows = pair ? 2 * mg::kBM : mg::kBM;   // output rows per tile
     const int b_rows = pair ? bn / 2 : bn;                // B rows (N) one CTA loads
 
