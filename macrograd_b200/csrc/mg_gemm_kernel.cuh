@@ -1153,10 +1153,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int unit0 = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
     const int unit_step = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
+    // split warps that report each landed stage to the MMA issuer: all of them
+    // when they compute lo tiles, else a single thread relays it
+    const int relay_threads = (p.split && !p.presplit) ? kSplitThreads : 1;
     if (threadIdx.x == 0) {
         for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(&ss->full[s]), 1);
-            mbar_init(smem_u32(&ss->split_done[s]), kSplitThreads * (kPair ? 2 : 1));
+            mbar_init(smem_u32(&ss->split_done[s]), relay_threads * (kPair ? 2 : 1));
             mbar_init(smem_u32(&ss->empty[s]), 1);
         }
         mbar_init(smem_u32(&ss->part_full), 1);
@@ -1486,15 +1489,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp >= kSplitWarp0) {
         // ------------------------------------------------ split / stage relay
-        // Every thread waits for the stage itself and reports it itself: a
-        // warp-wide wait / arrive is one warp instruction, and no thread is held
-        // back by another's wake-up (one elected arrival per warp or per CTA
-        // measured slower).
+        // When the warps split (3xTF32), every thread waits for the stage
+        // itself and reports its share itself: a warp-wide wait / arrive is one
+        // warp instruction, and no thread is held back by another's wake-up
+        // (one elected arrival per warp or per CTA measured slower there).
+        // With nothing to split, one thread relays each stage (relay_threads).
         const int tid = threadIdx.x - kSplitWarp0 * 32;
         const bool compute_lo = p.split && !p.presplit;
         int stage = 0;
         uint32_t phase = 0;
-        bool ok = true;
+        bool ok = tid < relay_threads;   // without lo tiles to compute, one thread relays
         Unit u;
         for (int ui = 0; ok && unit_at(p, unit0, unit_step, ui, u); ++ui) {
             for (int kb = u.kb0; kb < u.kb1; ++kb) {
