@@ -354,6 +354,32 @@ def test_k_split_with_accumulate(monkeypatch):
     assert_close(host(g), prev + dW, 0, "beta=1 split")
 
 
+@pytest.mark.parametrize("blocks", ["1", "2"])
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("sa,sb,ta,tb", [
+    ((3, 300, 96), (96, 200), False, False),     # M and N tails, short K, broadcast B
+    ((2, 129, 64), (2, 250, 64), False, True),   # transposed B, widths below 256
+    ((640, 1000), (1000, 72), False, False),     # long K, narrow N
+])
+def test_staging_blocks_forced(monkeypatch, blocks, mode, sa, sb, ta, tb):
+    """One or two epilogue staging blocks per warp (MG_GEMM_STAGE_BLOCKS;
+    with two, consecutive TMA stores of C alternate blocks and a store waits
+    only for the store before last), against the oracle."""
+    monkeypatch.setenv("MG_GEMM_STAGE_BLOCKS", blocks)
+    set_mode(mode)
+    A = ob.seeded_uniform(sa, 881)
+    B = ob.seeded_uniform(sb, 882)
+    assert_close(gpu_matmul(A, B, ta, tb), ob.oracle_matmul(A, B, ta, tb), mode, f"stage blocks {blocks}")
+    q = ob.seeded_normal((2, 3, 150, 40), 883, 0.0, 0.5)
+    k = ob.seeded_normal((2, 3, 150, 40), 884, 0.0, 0.5)
+    P = host(F.attention_scores(cuda(q), cuda(k), 0.25, causal=True))
+    mask = ob.oracle_causal_mask(150)
+    for b in range(2):
+        for h in range(3):
+            S = ob.oracle_matmul(q[b, h] * np.float32(0.25), k[b, h], False, True, mask)
+            assert_close(P[b, h], ob.oracle_softmax_rows(S), mode, f"softmax, stage blocks {blocks}")
+
+
 @pytest.mark.parametrize("bias_shape", [(40,), (1, 40), (30, 1), (30, 40), (3, 1, 40), (3, 30, 40)])
 def test_bias_broadcast_forms(bias_shape):
     set_mode(_lib.MG_MODE_TF32X3)
