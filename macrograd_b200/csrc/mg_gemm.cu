@@ -635,6 +635,21 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         }
     }
     gp.stages = stages;
+    // Narrow 3xTF32 tiles on one SM with K-major A: A's hi and lo tiles go to
+    // TMEM (written by the split warps, 64 columns a stage after the
+    // accumulators) and the MMAs read A there. Their three MMAs per K-step
+    // otherwise each read the whole 128-row A tile from shared memory for
+    // only 64-128 output columns, which sets the pace of the K loop.
+    // MG_GEMM_A_TMEM=0 keeps A in shared memory.
+    gp.a_tmem = 0;
+    gp.a_col0 = 0;
+    gp.tmem_cols = (int)L::kTmemCols;
+    if (split && !gp.presplit && !kPair && !gp.a_mn && BN <= 128 && 2 * BN + 64 * stages <= 512 &&
+        tuning_int("MG_GEMM_A_TMEM", 1, 0, 1)) {
+        gp.a_tmem = 1;
+        gp.a_col0 = 2 * BN;
+        gp.tmem_cols = (int)mg::pow2_at_least((uint32_t)(2 * BN + 64 * stages));
+    }
     const size_t smem = fixed + per_stage * stages;
     auto k = kernel_of<BN, kPair, kRow>();
     const int slot = bn_slot(BN) + (kPair ? 4 : 0);

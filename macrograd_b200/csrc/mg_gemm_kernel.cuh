@@ -124,6 +124,11 @@ struct GemmParams {
     int relay_spin;             // split warps poll without suspend hints
     int split;                  // 1 = 3xTF32
     int presplit;               // 3xTF32 with lo planes precomputed in HBM (tmAlo / tmBlo)
+    int a_tmem;                 // 3xTF32, K-major A, single SM: the split warps write each stage's
+                                // A hi and lo tiles into TMEM (columns a_col0 + 64 * stage) and
+                                // the MMAs read A from there; shared memory serves only B
+    int a_col0;                 // first TMEM column of those A tiles
+    int tmem_cols;              // TMEM columns allocated (a power of two >= 32)
     int dbuf;                   // every unit is one chunk: two accumulators, no promotion
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
     int a_rank, b_rank;         // tensor-map ranks (2 + mapped batch dims)
@@ -1192,10 +1197,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.c_tma && threadIdx.x == 0) tma_prefetch_map(&tmC);
     if (warp == kMmaWarp) {
         if (kPair) {
-            tmem_alloc_pair(smem_u32(&ss->tmem_base), L::kTmemCols);
+            tmem_alloc_pair(smem_u32(&ss->tmem_base), (uint32_t)p.tmem_cols);
             tmem_relinquish_pair();
         } else {
-            tmem_alloc(smem_u32(&ss->tmem_base), L::kTmemCols);
+            tmem_alloc(smem_u32(&ss->tmem_base), (uint32_t)p.tmem_cols);
             tmem_relinquish();
         }
     }
@@ -1355,7 +1360,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t accum = (!chunk_start || ks > 0) ? 1u : 0u;
                         const uint64_t da = smem_desc(a_raw(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t db = smem_desc(b_raw(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                        if (split) {
+                        if (!kPair && split && p.a_tmem) {
+                            // A's hi and lo tiles from TMEM (the split warps wrote them)
+                            const uint32_t t_hi = tmem_base + (uint32_t)(p.a_col0 + 64 * stage + 8 * ks);
+                            const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
+                            tc_mma_tf32_ta(d_tmem, t_hi + 32u, db, p.idesc, accum);   // lo * hi
+                            tc_mma_tf32_ta(d_tmem, t_hi, dbl, p.idesc, 1u);           // hi * lo
+                            tc_mma_tf32_ta(d_tmem, t_hi, db, p.idesc, 1u);            // hi * hi
+                        } else if (split) {
                             const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
                             mma(dal, db, accum);   // lo * hi
@@ -1509,7 +1521,44 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                if (compute_lo) {
+                if (compute_lo && !kPair && p.a_tmem) {
+                    // A into TMEM: this thread's row (TMEM lane tid: warp 8 + g
+                    // writes lanes 32g ..) out of the 128-byte-swizzled K-major
+                    // tile, as hi (truncated to TF32) and lo = x - hi, 32 columns each
+                    const uint4* arow = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) + tid * 8;
+                    uint32_t hi[32], lw[32];
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint4 x = arow[c ^ (tid & 7)];
+                        const uint32_t e[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            hi[4 * c + j] = e[j] & 0xFFFFE000u;
+                            lw[4 * c + j] = split_lo(e[j]);
+                        }
+                    }
+                    const uint32_t t_a = tmem_base + ((uint32_t)((tid >> 5) * 32) << 16) +
+                                         (uint32_t)(p.a_col0 + 64 * stage);
+                    tmem_st32_async(t_a, hi);
+                    tmem_st32_async(t_a + 32u, lw);
+                    // and the B tile's lo beside it in shared memory, as below
+                    const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) +
+                                       L::kABytes / 16;
+                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)stage * L::kStageBytes) +
+                                L::kABytes / 16;
+                    constexpr int n4 = (int)(L::kBBytes / 16);
+                    static_assert(n4 % kSplitThreads == 0, "B tile not a whole number of split rounds");
+                    constexpr int kPer = n4 / kSplitThreads;
+#pragma unroll
+                    for (int u = 0; u < kPer; ++u) {
+                        const uint4 x = raw[tid + u * kSplitThreads];
+                        lo[tid + u * kSplitThreads] =
+                            make_uint4(split_lo(x.x), split_lo(x.y), split_lo(x.z), split_lo(x.w));
+                    }
+                    fence_proxy_async_smem();
+                    tmem_wait_st();
+                    tc_fence_before();   // the TMEM writes before the MMA issuer's reads
+                } else if (compute_lo) {
                     // The MMA reads the raw tile as hi (the TF32 datapath drops the
                     // 13 low mantissa bits); lo = x - hi is exact.
                     const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes);
@@ -1747,8 +1796,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kPair) cluster_sync_all();   // the leader's MMAs no longer touch the peer
     if (warp == kMmaWarp) {
         tc_fence_after();
-        if (kPair) tmem_dealloc_pair(tmem_base, L::kTmemCols);
-        else tmem_dealloc(tmem_base, L::kTmemCols);
+        if (kPair) tmem_dealloc_pair(tmem_base, (uint32_t)p.tmem_cols);
+        else tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
     }
 }
 

@@ -270,6 +270,19 @@ __device__ __forceinline__ void tc_commit(uint32_t bar)
 // ---- CTA-pair forms (cta_group::2): the MMA of an M=256 tile runs on two SMs,
 // each holding 128 rows of A and half of the columns of B in shared memory and
 // 128 rows of D in its own TMEM.
+// As tc_mma_tf32, with the A operand (M = 128 lanes, one column per K
+// element) read from tensor memory at a_tmem instead of shared memory.
+__device__ __forceinline__ void tc_mma_tf32_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols)
 {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
