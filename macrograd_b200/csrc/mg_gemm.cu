@@ -254,7 +254,7 @@ bool tma_compatible(const Operand& x, const BatchMap& bm)
 }
 
 mg_status encode_map(CUtensorMap* map, const Operand& x, const BatchMap& bm, int box_rows_is_k,
-                     uint32_t box_outer)
+                     uint32_t box_outer, bool plain = false)
 {
     // dims: {cols (contiguous), rows, batch map dims...}
     cuuint64_t dims[5];
@@ -273,8 +273,10 @@ mg_status encode_map(CUtensorMap* map, const Operand& x, const BatchMap& bm, int
     box[0] = 32;
     box[1] = box_rows_is_k ? 32u : box_outer;
     // K-major boxes: 16-byte-chunk 128B swizzle; MN-major boxes: 32-byte-chunk
-    // 128B swizzle (the only MN-major layout the TF32 MMA reads).
-    const CUtensorMapSwizzle sw = box_rows_is_k ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+    // 128B swizzle (the only MN-major layout the TF32 MMA reads); `plain`: no
+    // swizzle, for an A tile that only the split warps read (A in TMEM).
+    const CUtensorMapSwizzle sw = plain ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                        : (box_rows_is_k ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
     CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank,
                           const_cast<float*>(x.ptr), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
@@ -635,18 +637,12 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
         }
     }
     gp.stages = stages;
-    // Narrow 3xTF32 tiles on one SM with K-major A: A's hi and lo tiles go to
-    // TMEM (written by the split warps, 64 columns a stage after the
-    // accumulators) and the MMAs read A there. Their three MMAs per K-step
-    // otherwise each read the whole 128-row A tile from shared memory for
-    // only 64-128 output columns, which sets the pace of the K loop.
-    // MG_GEMM_A_TMEM=0 keeps A in shared memory.
-    gp.a_tmem = 0;
+    // A in TMEM (gp.a_tmem, set with the maps): 64 columns a stage after the accumulators
     gp.a_col0 = 0;
     gp.tmem_cols = (int)L::kTmemCols;
-    if (split && !gp.presplit && !kPair && !gp.a_mn && BN <= 128 && 2 * BN + 64 * stages <= 512 &&
-        tuning_int("MG_GEMM_A_TMEM", 1, 0, 1)) {
-        gp.a_tmem = 1;
+    if (gp.a_tmem) {
+        stages = std::min(stages, (512 - 2 * BN) / 64);   // the A tiles' columns fit beside the accumulators
+        gp.stages = stages;
         gp.a_col0 = 2 * BN;
         gp.tmem_cols = (int)mg::pow2_at_least((uint32_t)(2 * BN + 64 * stages));
     }
@@ -1034,6 +1030,19 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const int64_t n_tiles_est = (d->N + bn - 1) / bn;
     const bool presplit = mode == MG_MODE_TF32X3 && arena == nullptr &&
                           want_presplit(2.0 * d->M * d->N * d->K * (double)all_batch, m_tiles_est, n_tiles_est);
+    // Narrow 3xTF32 tiles on one SM: A's hi and lo tiles go to TMEM (written
+    // by the split warps, 64 columns a stage after the accumulators) and the
+    // MMAs read A there. Their three MMAs per K-step otherwise each read the
+    // whole 128-row A tile from shared memory for only 64-128 output columns,
+    // which sets the pace of the K loop. Only the split warps then read A's
+    // shared-memory tile, so an MN-major A lands unswizzled (rows of M at
+    // 128-byte K steps). MG_GEMM_A_TMEM=0 keeps A in shared memory.
+    const bool a_tmem = mode == MG_MODE_TF32X3 && !presplit && !pair && bn <= 128 &&
+                        tuning_int("MG_GEMM_A_TMEM", 1, 0, 1);
+    if (a_tmem && a_mn) {
+        s = encode_map(&ma, a, am, a_mn, mg::kBM, true);
+        if (s != MG_OK) return s;
+    }
     CUtensorMap malo = ma, mblo = mb;
     if (presplit) {
         for (int which = 0; which < 2; ++which) {
@@ -1078,12 +1087,16 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.relay_spin = tuning_int("MG_GEMM_RELAY_SPIN", 0, 0, 1);
     gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
     gp.presplit = presplit ? 1 : 0;
+    gp.a_tmem = a_tmem ? 1 : 0;
     gp.a_mn = a_mn;
     gp.b_mn = b_mn;
     gp.a_rank = 2 + am.nmap;
     gp.b_rank = 2 + bmp.nmap;
-    // instruction descriptor: D f32, A/B tf32, majors, N = bn, M = 128 (one SM) or 256 (pair)
-    gp.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+    // instruction descriptor: D f32, A/B tf32, majors, N = bn, M = 128 (one SM) or 256 (pair).
+    // A read from TMEM (a_tmem) is always K-major there (lane = row, column = K),
+    // whatever its layout in memory: the MN-major flag with a TMEM A operand is
+    // an illegal instruction.
+    gp.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(a_mn && !a_tmem) << 15) | ((uint32_t)b_mn << 16) |
                ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(tile_rows >> 4) << 24);
     gp.nbd = nbd;
     for (int i = 0; i < mg::kMaxBatchDims; ++i) {

@@ -1523,19 +1523,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (compute_lo && !kPair && p.a_tmem) {
                     // A into TMEM: this thread's row (TMEM lane tid: warp 8 + g
-                    // writes lanes 32g ..) out of the 128-byte-swizzled K-major
-                    // tile, as hi (truncated to TF32) and lo = x - hi, 32 columns each
-                    const uint4* arow = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) + tid * 8;
+                    // writes lanes 32g ..) as hi (truncated to TF32) and
+                    // lo = x - hi, 32 columns each; from the 128-byte-swizzled
+                    // K-major tile, or the unswizzled MN-major one (32-row boxes
+                    // of 4 KB, K steps of 128 bytes)
                     uint32_t hi[32], lw[32];
+                    if (!p.a_mn) {
+                        const uint4* arow = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) + tid * 8;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint4 x = arow[c ^ (tid & 7)];
-                        const uint32_t e[4] = {x.x, x.y, x.z, x.w};
+                        for (int c = 0; c < 8; ++c) {
+                            const uint4 x = arow[c ^ (tid & 7)];
+                            const uint32_t e[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            hi[4 * c + j] = e[j] & 0xFFFFE000u;
-                            lw[4 * c + j] = split_lo(e[j]);
+                            for (int j = 0; j < 4; ++j) hi[4 * c + j] = e[j];
                         }
+                    } else {
+                        const uint32_t* acol = reinterpret_cast<const uint32_t*>(smem + (size_t)stage * L::kStageBytes) +
+                                               (tid >> 5) * 1024 + (tid & 31);
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) hi[k] = acol[k * 32];
+                    }
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) {
+                        lw[k] = split_lo(hi[k]);
+                        hi[k] &= 0xFFFFE000u;
                     }
                     const uint32_t t_a = tmem_base + ((uint32_t)((tid >> 5) * 32) << 16) +
                                          (uint32_t)(p.a_col0 + 64 * stage);
