@@ -611,7 +611,8 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
 {
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
-    const size_t per_stage = (size_t)L::kStageBytes * (split ? 2 : 1);   // raw (+ lo) tiles
+    // raw (+ lo) tiles; with A in TMEM only B's lo tile sits beside each stage
+    const size_t per_stage = (size_t)L::kStageBytes + (split ? (gp.a_tmem ? L::kBBytes : L::kStageBytes) : 0);
     // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
     // (+ the softmax backward's P ring, when two operand stages still fit)
     size_t fixed = 1024 + mg::kSharedStateBytes + (size_t)mg::kEpiWarps * mg::kStageFloatsPerWarp * 4 + 64;
@@ -641,7 +642,8 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     gp.a_col0 = 0;
     gp.tmem_cols = (int)L::kTmemCols;
     if (gp.a_tmem) {
-        stages = std::min(stages, (512 - 2 * BN) / 64);   // the A tiles' columns fit beside the accumulators
+        // the A tiles' columns fit beside the accumulators (MG_GEMM_A_TMEM_STAGES caps them)
+        stages = std::min(stages, std::min((512 - 2 * BN) / 64, tuning_int("MG_GEMM_A_TMEM_STAGES", 8, 2, 8)));
         gp.stages = stages;
         gp.a_col0 = 2 * BN;
         gp.tmem_cols = (int)mg::pow2_at_least((uint32_t)(2 * BN + 64 * stages));

@@ -1142,13 +1142,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t smem_base = smem_u32(smem);
     const int stages = p.stages;
     // shared memory: raw stages, then (3xTF32) one lo tile per stage, then the barriers
+    // (with A in TMEM the lo region holds only B's lo tiles, kBBytes a stage)
     const uint32_t raw_region = (uint32_t)stages * L::kStageBytes;
-    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region * (p.split ? 2u : 1u));
+    const uint32_t lo_stride = p.a_tmem ? L::kBBytes : L::kStageBytes;
+    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region + (p.split ? (uint32_t)stages * lo_stride : 0u));
 
     auto a_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes; };
     auto b_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes + L::kABytes; };
     auto a_lo = [&](int s) { return a_raw(s) + raw_region; };
-    auto b_lo = [&](int s) { return b_raw(s) + raw_region; };
+    auto b_lo = [&](int s) {
+        return p.a_tmem ? smem_base + raw_region + (uint32_t)s * L::kBBytes : b_raw(s) + raw_region;
+    };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -1555,8 +1559,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // and the B tile's lo beside it in shared memory, as below
                     const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) +
                                        L::kABytes / 16;
-                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)stage * L::kStageBytes) +
-                                L::kABytes / 16;
+                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)stage * L::kBBytes);
                     constexpr int n4 = (int)(L::kBBytes / 16);
                     static_assert(n4 % kSplitThreads == 0, "B tile not a whole number of split rounds");
                     constexpr int kPer = n4 / kSplitThreads;
