@@ -1032,15 +1032,15 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     const int64_t n_tiles_est = (d->N + bn - 1) / bn;
     const bool presplit = mode == MG_MODE_TF32X3 && arena == nullptr &&
                           want_presplit(2.0 * d->M * d->N * d->K * (double)all_batch, m_tiles_est, n_tiles_est);
-    // Narrow 3xTF32 tiles on one SM: A's hi and lo tiles go to TMEM (written
+    // Narrow 3xTF32 tiles (single SM or pair): A's hi and lo tiles go to TMEM (written
     // by the split warps, 64 columns a stage after the accumulators) and the
     // MMAs read A there. Their three MMAs per K-step otherwise each read the
     // whole 128-row A tile from shared memory for only 64-128 output columns,
     // which sets the pace of the K loop. Only the split warps then read A's
     // shared-memory tile, so an MN-major A lands unswizzled (rows of M at
     // 128-byte K steps). MG_GEMM_A_TMEM=0 keeps A in shared memory.
-    const bool a_tmem = mode == MG_MODE_TF32X3 && !presplit && !pair && bn <= 128 &&
-                        tuning_int("MG_GEMM_A_TMEM", 1, 0, 1);
+    const bool a_tmem = mode == MG_MODE_TF32X3 && !presplit && bn <= 128 &&
+                        tuning_int("MG_GEMM_A_TMEM", 1, 0, 1) && (!pair || tuning_int("MG_GEMM_A_TMEM_PAIR", 1, 0, 1));
     if (a_tmem && a_mn) {
         s = encode_map(&ma, a, am, a_mn, mg::kBM, true);
         if (s != MG_OK) return s;

@@ -1364,13 +1364,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t accum = (!chunk_start || ks > 0) ? 1u : 0u;
                         const uint64_t da = smem_desc(a_raw(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t db = smem_desc(b_raw(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                        if (!kPair && split && p.a_tmem) {
-                            // A's hi and lo tiles from TMEM (the split warps wrote them)
+                        if (split && p.a_tmem) {
+                            // A's hi and lo tiles from TMEM (the split warps wrote them;
+                            // in a pair each CTA's rows in its own TMEM)
                             const uint32_t t_hi = tmem_base + (uint32_t)(p.a_col0 + 64 * stage + 8 * ks);
                             const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                            tc_mma_tf32_ta(d_tmem, t_hi + 32u, db, p.idesc, accum);   // lo * hi
-                            tc_mma_tf32_ta(d_tmem, t_hi, dbl, p.idesc, 1u);           // hi * lo
-                            tc_mma_tf32_ta(d_tmem, t_hi, db, p.idesc, 1u);            // hi * hi
+                            auto mma_ta = [&](uint32_t ta, uint64_t db_, uint32_t acc) {
+                                if (kPair) tc_mma_tf32_pair_ta(d_tmem, ta, db_, p.idesc, acc);
+                                else tc_mma_tf32_ta(d_tmem, ta, db_, p.idesc, acc);
+                            };
+                            mma_ta(t_hi + 32u, db, accum);   // lo * hi
+                            mma_ta(t_hi, dbl, 1u);           // hi * lo
+                            mma_ta(t_hi, db, 1u);            // hi * hi
                         } else if (split) {
                             const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
@@ -1525,7 +1530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                if (compute_lo && !kPair && p.a_tmem) {
+                if (compute_lo && p.a_tmem) {
                     // A into TMEM: this thread's row (TMEM lane tid: warp 8 + g
                     // writes lanes 32g ..) as hi (truncated to TF32) and
                     // lo = x - hi, 32 columns each; from the 128-byte-swizzled

@@ -301,6 +301,19 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
                  : "memory");
 }
 
+// As tc_mma_tf32_pair, with A read from the tensor memory of both CTAs of the
+// pair at a_tmem (each CTA's 128 rows in its own lanes).
+__device__ __forceinline__ void tc_mma_tf32_pair_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                    uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_mma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                                  uint32_t idesc, uint32_t accumulate)
 {
