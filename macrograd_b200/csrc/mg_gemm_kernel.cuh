@@ -124,7 +124,7 @@ struct GemmParams {
     int relay_spin;             // split warps poll without suspend hints
     int split;                  // 1 = 3xTF32
     int presplit;               // 3xTF32 with lo planes precomputed in HBM (tmAlo / tmBlo)
-    int a_tmem;                 // 3xTF32, K-major A, single SM: the split warps write each stage's
+    int a_tmem;                 // 3xTF32, tiles up to 128 wide: the split warps write each stage's
                                 // A hi and lo tiles into TMEM (columns a_col0 + 64 * stage) and
                                 // the MMAs read A from there; shared memory serves only B
     int a_col0;                 // first TMEM column of those A tiles
@@ -1135,6 +1135,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                       const __grid_constant__ PeerMaps pm)
 {
     using L = Layout<BN, kPair>;
+    // A in TMEM (p.a_tmem) exists for tiles up to 128 wide only: the wider
+    // instantiations compile without any of its branches
+    constexpr bool kATmem = BN <= 128;
+    const bool a_tmem = kATmem && p.a_tmem != 0;
+    const uint32_t tmem_cols = kATmem ? (uint32_t)p.tmem_cols : L::kTmemCols;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -1144,14 +1149,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // shared memory: raw stages, then (3xTF32) one lo tile per stage, then the barriers
     // (with A in TMEM the lo region holds only B's lo tiles, kBBytes a stage)
     const uint32_t raw_region = (uint32_t)stages * L::kStageBytes;
-    const uint32_t lo_stride = p.a_tmem ? L::kBBytes : L::kStageBytes;
+    const uint32_t lo_stride = a_tmem ? L::kBBytes : L::kStageBytes;
     SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region + (p.split ? (uint32_t)stages * lo_stride : 0u));
 
     auto a_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes; };
     auto b_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes + L::kABytes; };
     auto a_lo = [&](int s) { return a_raw(s) + raw_region; };
     auto b_lo = [&](int s) {
-        return p.a_tmem ? smem_base + raw_region + (uint32_t)s * L::kBBytes : b_raw(s) + raw_region;
+        return a_tmem ? smem_base + raw_region + (uint32_t)s * L::kBBytes : b_raw(s) + raw_region;
     };
 
     const int warp = threadIdx.x >> 5;
@@ -1201,10 +1206,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (p.c_tma && threadIdx.x == 0) tma_prefetch_map(&tmC);
     if (warp == kMmaWarp) {
         if (kPair) {
-            tmem_alloc_pair(smem_u32(&ss->tmem_base), (uint32_t)p.tmem_cols);
+            tmem_alloc_pair(smem_u32(&ss->tmem_base), tmem_cols);
             tmem_relinquish_pair();
         } else {
-            tmem_alloc(smem_u32(&ss->tmem_base), (uint32_t)p.tmem_cols);
+            tmem_alloc(smem_u32(&ss->tmem_base), tmem_cols);
             tmem_relinquish();
         }
     }
@@ -1364,7 +1369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const uint32_t accum = (!chunk_start || ks > 0) ? 1u : 0u;
                         const uint64_t da = smem_desc(a_raw(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t db = smem_desc(b_raw(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                        if (split && p.a_tmem) {
+                        if (split && a_tmem) {
                             // A's hi and lo tiles from TMEM (the split warps wrote them;
                             // in a pair each CTA's rows in its own TMEM)
                             const uint32_t t_hi = tmem_base + (uint32_t)(p.a_col0 + 64 * stage + 8 * ks);
@@ -1530,7 +1535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                if (compute_lo && p.a_tmem) {
+                if (compute_lo && a_tmem) {
                     // A into TMEM: this thread's row (TMEM lane tid: warp 8 + g
                     // writes lanes 32g ..) as hi (truncated to TF32) and
                     // lo = x - hi, 32 columns each; from the 128-byte-swizzled
@@ -1815,8 +1820,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (kPair) cluster_sync_all();   // the leader's MMAs no longer touch the peer
     if (warp == kMmaWarp) {
         tc_fence_after();
-        if (kPair) tmem_dealloc_pair(tmem_base, (uint32_t)p.tmem_cols);
-        else tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+        if (kPair) tmem_dealloc_pair(tmem_base, tmem_cols);
+        else tmem_dealloc(tmem_base, tmem_cols);
     }
 }
 
