@@ -612,6 +612,7 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     using L = mg::Layout<BN, kPair>;
     const int split = gp.split;
     // raw (+ lo) tiles; with A in TMEM only B's lo tile sits beside each stage
+    // (b2: inside the stage, right after B)
     const size_t per_stage = (size_t)L::kStageBytes + (split ? (gp.a_tmem ? L::kBBytes : L::kStageBytes) : 0);
     // alignment slack + barriers + the epilogue's store staging (4 KB per warp)
     // (+ the softmax backward's P ring, when two operand stages still fit)
@@ -642,11 +643,13 @@ mg_status launch_tc(DeviceState* dev, const CUtensorMap& ma, const CUtensorMap& 
     gp.a_col0 = 0;
     gp.tmem_cols = (int)L::kTmemCols;
     if (gp.a_tmem) {
-        // the A tiles' columns fit beside the accumulators (MG_GEMM_A_TMEM_STAGES caps them)
-        stages = std::min(stages, std::min((512 - 2 * BN) / 64, tuning_int("MG_GEMM_A_TMEM_STAGES", 8, 2, 8)));
+        // the A tiles' columns fit beside the two accumulators (2 BN wide each with b2)
+        // (MG_GEMM_A_TMEM_STAGES caps them)
+        const int acc_cols = 2 * BN * (gp.b2 ? 2 : 1);
+        stages = std::min(stages, std::min((512 - acc_cols) / 64, tuning_int("MG_GEMM_A_TMEM_STAGES", 8, 2, 8)));
         gp.stages = stages;
-        gp.a_col0 = 2 * BN;
-        gp.tmem_cols = (int)mg::pow2_at_least((uint32_t)(2 * BN + 64 * stages));
+        gp.a_col0 = acc_cols;
+        gp.tmem_cols = (int)mg::pow2_at_least((uint32_t)(acc_cols + 64 * stages));
     }
     const size_t smem = fixed + per_stage * stages;
     auto k = kernel_of<BN, kPair, kRow>();
@@ -1090,6 +1093,13 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     gp.split = mode == MG_MODE_TF32X3 ? 1 : 0;
     gp.presplit = presplit ? 1 : 0;
     gp.a_tmem = a_tmem ? 1 : 0;
+    // width 64 with A in TMEM and a plain epilogue: B's lo tile right after B's
+    // in the stage, so [B hi | B lo] is one operand 128 wide and a K-step is two
+    // MMAs (A hi, A lo) instead of three -- each MMA costs about the same time
+    // at widths up to 128, so the K loop's MMAs take two thirds of the time.
+    // MG_GEMM_B2=0 keeps three MMAs of width 64.
+    gp.b2 = (a_tmem && !pair && bn == 64 && (d->epilogue & (MG_EPI_SOFTMAX | mg::kEpiSoftmaxBwd)) == 0 &&
+             tuning_int("MG_GEMM_B2", 1, 0, 1)) ? 1 : 0;
     gp.a_mn = a_mn;
     gp.b_mn = b_mn;
     gp.a_rank = 2 + am.nmap;
@@ -1100,6 +1110,7 @@ static mg_status gemm_impl(const mg_gemm_desc* d, float* C, const float* A, cons
     // an illegal instruction.
     gp.idesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(a_mn && !a_tmem) << 15) | ((uint32_t)b_mn << 16) |
                ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(tile_rows >> 4) << 24);
+    gp.idesc2 = (gp.idesc & ~(0x3Fu << 17)) | ((uint32_t)((2 * bn) >> 3) << 17);   // N = 2 bn (b2)
     gp.nbd = nbd;
     for (int i = 0; i < mg::kMaxBatchDims; ++i) {
         gp.bsize[i] = i < nbd && !red[i] ? d->batch[i] : 1;

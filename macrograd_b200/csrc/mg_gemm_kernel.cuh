@@ -128,6 +128,11 @@ struct GemmParams {
                                 // A hi and lo tiles into TMEM (columns a_col0 + 64 * stage) and
                                 // the MMAs read A from there; shared memory serves only B
     int a_col0;                 // first TMEM column of those A tiles
+    int b2;                     // with A in TMEM, width 64, plain epilogue: B's lo tile follows B's
+                                // tile in the stage, and each K-step is two MMAs of width 2 BN
+                                // (A hi, then A lo, times [B hi | B lo]); the accumulator is 2 BN
+                                // wide and its two halves are added for the result
+    uint32_t idesc2;            // instruction descriptor of those width-2 BN MMAs
     int tmem_cols;              // TMEM columns allocated (a power of two >= 32)
     int dbuf;                   // every unit is one chunk: two accumulators, no promotion
     int a_mn, b_mn;             // 1 = operand tile is MN-major (transposed view)
@@ -1140,6 +1145,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr bool kATmem = BN <= 128;
     const bool a_tmem = kATmem && p.a_tmem != 0;
     const uint32_t tmem_cols = kATmem ? (uint32_t)p.tmem_cols : L::kTmemCols;
+    // p.b2 exists for the single-SM plain-epilogue kernel of width 64 only
+    constexpr bool kB2 = BN == 64 && !kPair && kRow == kRowNone;
+    const bool b2 = kB2 && a_tmem && p.b2 != 0;
+    const uint32_t acc_w = b2 ? 2u * BN : (uint32_t)BN;   // TMEM columns of one accumulator
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128-byte swizzle atoms.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -1148,15 +1157,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int stages = p.stages;
     // shared memory: raw stages, then (3xTF32) one lo tile per stage, then the barriers
     // (with A in TMEM the lo region holds only B's lo tiles, kBBytes a stage)
-    const uint32_t raw_region = (uint32_t)stages * L::kStageBytes;
+    // (with b2 each stage is A, B, B's lo tile, and there is no lo region)
+    const uint32_t stage_stride = b2 ? L::kStageBytes + L::kBBytes : L::kStageBytes;
+    const uint32_t raw_region = (uint32_t)stages * stage_stride;
     const uint32_t lo_stride = a_tmem ? L::kBBytes : L::kStageBytes;
-    SharedState* ss = reinterpret_cast<SharedState*>(smem + raw_region + (p.split ? (uint32_t)stages * lo_stride : 0u));
+    SharedState* ss =
+        reinterpret_cast<SharedState*>(smem + raw_region + (p.split && !b2 ? (uint32_t)stages * lo_stride : 0u));
 
-    auto a_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes; };
-    auto b_raw = [&](int s) { return smem_base + (uint32_t)s * L::kStageBytes + L::kABytes; };
+    auto a_raw = [&](int s) { return smem_base + (uint32_t)s * stage_stride; };
+    auto b_raw = [&](int s) { return smem_base + (uint32_t)s * stage_stride + L::kABytes; };
     auto a_lo = [&](int s) { return a_raw(s) + raw_region; };
     auto b_lo = [&](int s) {
-        return a_tmem ? smem_base + raw_region + (uint32_t)s * L::kBBytes : b_raw(s) + raw_region;
+        return b2 ? b_raw(s) + L::kBBytes
+                  : (a_tmem ? smem_base + raw_region + (uint32_t)s * L::kBBytes : b_raw(s) + raw_region);
     };
 
     const int warp = threadIdx.x >> 5;
@@ -1342,7 +1355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // accumulators, so a tile's MMAs run during the previous
                 // tile's epilogue
                 const int rg = p.dbuf ? (ui & 1) : 0;
-                d_tmem = tmem_base + (uint32_t)(rg * BN);
+                d_tmem = tmem_base + (uint32_t)rg * acc_w;
                 const uint32_t acc_free = smem_u32(rg ? &ss->part_free1 : &ss->part_free);
                 const uint32_t acc_full = smem_u32(rg ? &ss->part_full1 : &ss->part_full);
                 for (int kb = u.kb0; kb < u.kb1; ++kb) {
@@ -1373,14 +1386,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // A's hi and lo tiles from TMEM (the split warps wrote them;
                             // in a pair each CTA's rows in its own TMEM)
                             const uint32_t t_hi = tmem_base + (uint32_t)(p.a_col0 + 64 * stage + 8 * ks);
-                            const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
-                            auto mma_ta = [&](uint32_t ta, uint64_t db_, uint32_t acc) {
-                                if (kPair) tc_mma_tf32_pair_ta(d_tmem, ta, db_, p.idesc, acc);
-                                else tc_mma_tf32_ta(d_tmem, ta, db_, p.idesc, acc);
+                            auto mma_ta = [&](uint32_t ta, uint64_t db_, uint32_t acc, uint32_t idesc) {
+                                if (kPair) tc_mma_tf32_pair_ta(d_tmem, ta, db_, idesc, acc);
+                                else tc_mma_tf32_ta(d_tmem, ta, db_, idesc, acc);
                             };
-                            mma_ta(t_hi + 32u, db, accum);   // lo * hi
-                            mma_ta(t_hi, dbl, 1u);           // hi * lo
-                            mma_ta(t_hi, db, 1u);            // hi * hi
+                            if (b2) {
+                                // [B hi | B lo] is one operand 2 BN wide (db): two MMAs
+                                // give hi*hi | hi*lo and add lo*hi | lo*lo
+                                mma_ta(t_hi, db, accum, p.idesc2);
+                                mma_ta(t_hi + 32u, db, 1u, p.idesc2);
+                            } else {
+                                const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
+                                mma_ta(t_hi + 32u, db, accum, p.idesc);   // lo * hi
+                                mma_ta(t_hi, dbl, 1u, p.idesc);           // hi * lo
+                                mma_ta(t_hi, db, 1u, p.idesc);            // hi * hi
+                            }
                         } else if (split) {
                             const uint64_t dal = smem_desc(a_lo(stage) + ks * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t dbl = smem_desc(b_lo(stage) + ks * b_kstep, b_lbo, b_sbo, b_lay);
@@ -1543,7 +1563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // of 4 KB, K steps of 128 bytes)
                     uint32_t hi[32], lw[32];
                     if (!p.a_mn) {
-                        const uint4* arow = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) + tid * 8;
+                        const uint4* arow = reinterpret_cast<const uint4*>(smem + (size_t)stage * stage_stride) + tid * 8;
 #pragma unroll
                         for (int c = 0; c < 8; ++c) {
                             const uint4 x = arow[c ^ (tid & 7)];
@@ -1552,7 +1572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int j = 0; j < 4; ++j) hi[4 * c + j] = e[j];
                         }
                     } else {
-                        const uint32_t* acol = reinterpret_cast<const uint32_t*>(smem + (size_t)stage * L::kStageBytes) +
+                        const uint32_t* acol = reinterpret_cast<const uint32_t*>(smem + (size_t)stage * stage_stride) +
                                                (tid >> 5) * 1024 + (tid & 31);
 #pragma unroll
                         for (int k = 0; k < 32; ++k) hi[k] = acol[k * 32];
@@ -1567,9 +1587,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tmem_st32_async(t_a, hi);
                     tmem_st32_async(t_a + 32u, lw);
                     // and the B tile's lo beside it in shared memory, as below
-                    const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * L::kStageBytes) +
+                    const uint4* raw = reinterpret_cast<const uint4*>(smem + (size_t)stage * stage_stride) +
                                        L::kABytes / 16;
-                    uint4* lo = reinterpret_cast<uint4*>(smem + raw_region + (size_t)stage * L::kBBytes);
+                    uint4* lo = b2 ? const_cast<uint4*>(raw) + L::kBBytes / 16   // right after B (b2)
+                                   : reinterpret_cast<uint4*>(smem + raw_region + (size_t)stage * L::kBBytes);
                     constexpr int n4 = (int)(L::kBBytes / 16);
                     static_assert(n4 % kSplitThreads == 0, "B tile not a whole number of split rounds");
                     constexpr int kPer = n4 / kSplitThreads;
@@ -1622,7 +1643,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row = sub * 32 + lane;
         const uint32_t lane_base = tmem_base + ((uint32_t)(sub * 32) << 16);
         const uint32_t t_part = lane_base;
-        const uint32_t t_master = lane_base + (uint32_t)BN;
+        const uint32_t t_master = lane_base + acc_w;   // (b2: the partial is 2 BN wide)
         float* stage_w = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ss) + kSharedStateBytes) +
                          warp * p.stage_blocks * kStageFloatsPerWarp;   // this warp's store staging block(s)
         const bool has_bias = (p.epi & kEpiBias) != 0;
@@ -1661,7 +1682,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // for until the partial has been released
                 for (int j = 32 * c_lo; j < 32 * c_hi; j += 32) {
                     uint32_t r[32];
-                    if (c > 0) {
+                    if (b2) {
+                        // the partial's two halves first (hi * B | lo * B terms)
+                        uint32_t q[32];
+                        tmem_ld32x2(t_part + j, r, t_part + (uint32_t)BN + j, q);
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            r[i] = __float_as_uint(__uint_as_float(r[i]) + __uint_as_float(q[i]));
+                        if (c > 0) {
+                            tmem_ld32(t_master + j, q);
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                r[i] = __float_as_uint(__uint_as_float(q[i]) + __uint_as_float(r[i]));
+                        }
+                    } else if (c > 0) {
                         uint32_t m[32];
                         tmem_ld32x2(t_part + j, r, t_master + j, m);
 #pragma unroll
@@ -1684,7 +1718,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (u.kind == 1) {
                 // A partial K-range: the master goes to its workspace slot for
                 // the tile's final range to add; nothing is written to C.
-                store_partial(p.part_ws + (size_t)(u.slot * 2 + (int)rank) * (kBM * BN), lane_base + (uint32_t)BN,
+                store_partial(p.part_ws + (size_t)(u.slot * 2 + (int)rank) * (kBM * BN), t_master,
                               c_lo, c_hi, row);
                 __threadfence();
                 __syncwarp();
@@ -1710,7 +1744,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __threadfence();
                 // master += the other ranges' partials, in range order
                 add_partials(p.part_ws + (size_t)(u.slot * 2 + (int)rank) * (kBM * BN), u.nsib,
-                             (size_t)2 * kBM * BN, lane_base + (uint32_t)BN, c_lo, c_hi, row);
+                             (size_t)2 * kBM * BN, t_master, c_lo, c_hi, row);
             }
 
             // ---- output epilogue from the master
@@ -1738,7 +1772,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             float* crow = p.C + coff + crow_idx * p.ldc;
             const float* brow = has_bias ? p.bias + boff + (int64_t)(rok ? gm : 0) * p.bias_rs : nullptr;
             // the result, column 0: the master, or (p.dbuf) this tile's accumulator
-            const uint32_t t_row = lane_base + (uint32_t)(p.dbuf ? rg * BN : BN);
+            const uint32_t t_row = p.dbuf ? lane_base + (uint32_t)rg * acc_w : t_master;
+            // b2 with one chunk: the accumulator's two halves are added here
+            const bool sum_halves = b2 && p.dbuf;
 
             if constexpr (softmax) {
                 // row softmax (N <= BN, one n-tile): softmax_tile
@@ -1762,11 +1798,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int gn0 = n0 + c;
                     if (gn0 >= p.N) break;   // uniform across the warp
                     uint32_t r[32];
-                    tmem_ld32(t_row + c, r);
-                    const int nvalid = min(32, p.N - gn0);
                     float v[32];
+                    if (sum_halves) {
+                        uint32_t q[32];
+                        tmem_ld32x2(t_row + c, r, t_row + (uint32_t)BN + c, q);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+                        for (int j = 0; j < 32; ++j)
+                            v[j] = p.alpha * (__uint_as_float(r[j]) + __uint_as_float(q[j]));
+                    } else {
+                        tmem_ld32(t_row + c, r);
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+                    }
+                    const int nvalid = min(32, p.N - gn0);
                     if (rok && has_bias) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)

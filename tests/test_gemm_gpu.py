@@ -354,6 +354,28 @@ def test_k_split_with_accumulate(monkeypatch):
     assert_close(host(g), prev + dW, 0, "beta=1 split")
 
 
+@pytest.mark.parametrize("b2", ["1", "0"])
+@pytest.mark.parametrize("sa,sb,ta,tb", [
+    ((100, 1000), (1000, 50), False, False),     # one m-tile, K over 4 promotion chunks
+    ((1000, 100), (50, 1000), True, True),       # both operands transposed views
+    ((3, 128, 256), (3, 256, 64), False, False), # batched, one chunk (two accumulators)
+    ((3, 256, 128), (3, 256, 40), True, False),  # MN-major A, N tail
+])
+def test_narrow_tiles_a_in_tmem(monkeypatch, b2, sa, sb, ta, tb):
+    """3xTF32 tiles of width 64 with A in tensor memory: [B hi | B lo] as one
+    operand of width 128 (two MMAs a K-step, the accumulator's halves added)
+    or three MMAs of width 64 (MG_GEMM_B2=0); with promotion chunks and with
+    two accumulators, against the oracle. The pre-split A/B path agrees."""
+    monkeypatch.setenv("MG_GEMM_B2", b2)
+    set_mode(_lib.MG_MODE_TF32X3)
+    A = ob.seeded_uniform(sa, 891)
+    B = ob.seeded_uniform(sb, 892)
+    ref = ob.oracle_matmul(A, B, ta, tb)
+    assert_close(gpu_matmul(A, B, ta, tb), ref, _lib.MG_MODE_TF32X3, f"b2={b2}")
+    monkeypatch.setenv("MG_GEMM_A_TMEM", "0")
+    assert_close(gpu_matmul(A, B, ta, tb), ref, _lib.MG_MODE_TF32X3, "A in shared memory")
+
+
 @pytest.mark.parametrize("blocks", ["1", "2"])
 @pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("sa,sb,ta,tb", [
