@@ -427,7 +427,7 @@ struct Layout {
     static constexpr uint32_t kABytes = kBM * 128;          // 16 KB
     static constexpr uint32_t kBBytes = kBBoxes * 32 * 128;  // room for whole MN-major boxes
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kTmemCols = pow2_at_least(2 * BN);   // partial + master
+    static constexpr uint32_t kTmemCols = pow2_at_least(2 * BN);   // partial + master (A in TMEM: p.tmem_cols)
     static constexpr int kTileRows = kPair ? 2 * kBM : kBM;  // output rows per tile
     static constexpr int kChunks = BN / 32;                  // 32-column epilogue chunks
     static constexpr int kHalfChunks = (kChunks + 1) / 2;    // chunks of column half 0
@@ -1155,9 +1155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
     const uint32_t smem_base = smem_u32(smem);
     const int stages = p.stages;
-    // shared memory: raw stages, then (3xTF32) one lo tile per stage, then the barriers
-    // (with A in TMEM the lo region holds only B's lo tiles, kBBytes a stage)
-    // (with b2 each stage is A, B, B's lo tile, and there is no lo region)
+    // shared memory: raw stages, then (3xTF32) one lo tile per stage, then the
+    // barriers; with A in TMEM the lo region holds only B's lo tiles (kBBytes a
+    // stage), and with b2 each stage is A, B, B's lo tile and there is no lo region
     const uint32_t stage_stride = b2 ? L::kStageBytes + L::kBBytes : L::kStageBytes;
     const uint32_t raw_region = (uint32_t)stages * stage_stride;
     const uint32_t lo_stride = a_tmem ? L::kBBytes : L::kStageBytes;
